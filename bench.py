@@ -1,0 +1,402 @@
+"""Benchmark of the decode hot path: batch-1 group-quantized GEMV.
+
+Workload: INT8 weights, group size 64, symmetric fp32
+group scales, from N(0, 0.02)-like synthetic values; activations fp32
+~N(0,1) quantized per 64-group inside the GEMV; Llama-2-7B layer shapes
+(n, d) = (4096, 4096) x4 [wq wk wv wo], (4096, 11008) x2 [w1 w3],
+(11008, 4096) [w2], (4096, 32000) [classifier].  One step = one pass over
+the eight products (eight kernel launches), captured in a CUDA graph with
+programmatic dependent launch; two copies of every matrix (0.71 GB in all,
+over 5x the 126 MB L2) alternate between steps so every weight byte comes
+from HBM.
+
+Metric: GB/s of algorithmic bytes (weights + scales + fp32 x in + fp32 y
+out, each byte once) over the timed steps, summed over ranks.  One process
+per GPU (torchrun for N > 1); every rank runs the same sweep on its own GPU
+(replicas: a batch-1 GEMV does not shard), timing = max over ranks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+--impl reference times the reference's own CPU path (runq.c matmul_q8,
+compiled from its sources into oracle/_ref/librunq.so; group size 32, the
+only one it supports) on the same shapes with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+SHAPES = [(4096, 4096)] * 4 + [(4096, 11008)] * 2 + [(11008, 4096), (4096, 32000)]  # (n, d)
+GS = 64
+KIND = 8
+COPIES = 2
+METRIC = "quantized-GEMV HBM GB/s (INT8 GS64 batch-1 sweep over Llama-2-7B layer shapes)"
+WORKLOAD = "config2: int8 gs64 batch-1 GEMV sweep, llama-2-7b shapes (wq,wk,wv,wo,w1,w3,w2,wcls)"
+
+
+def gemv_bytes(n: int, d: int, gs: int, kind: int, act_bytes_per_elem: float = 4.0) -> int:
+    wb = d * n if kind == 8 else d * n // 2
+    return int(wb + d * (n // gs) * 4 + n * act_bytes_per_elem + 4 * d)
+
+
+def step_bytes() -> int:
+    return sum(gemv_bytes(n, d, GS, KIND) for n, d in SHAPES)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes per GEMV launch from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"lq_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.gpu)], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        time.sleep(0.2)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.remove(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's runq.c matmul_q8 (or the scalar oracle)
+
+def cpu_has_vnni() -> bool:
+    try:
+        flags = open("/proc/cpuinfo").read()
+    except Exception:
+        return False
+    return all(f in flags for f in ("avx512_vnni", "avx512vl", "avx512bw", "avx512f"))
+
+
+def cpu_baseline(seconds: float = 10.0, steps: int | None = None, warmup: int = 0):
+    """Returns (GB/s, kind, cores, sample description, per-step seconds)."""
+    import oracle as O
+
+    rng = np.random.default_rng(0)
+    use_ref = O.ref_available() and cpu_has_vnni()
+    cores = os.cpu_count() or 1
+    if use_ref:
+        O.ref().ref_set_threads(cores)
+        mats = []
+        for n, d in SHAPES:
+            q = rng.integers(0, 256, size=(d, n), dtype=np.uint8)
+            s = (rng.random((d, n // 32), dtype=np.float32) * 1e-3).astype(np.float32)
+            x = rng.standard_normal(n).astype(np.float32)
+            xq, xs, xt = O.ref_quantize_act(x)
+            mats.append((n, d, q, s, xq, xs, xt))
+        per = sum(gemv_bytes(n, d, 32, 8, 1 + 8 / 32) for n, d in SHAPES)
+
+        def one():
+            for n, d, q, s, xq, xs, xt in mats:
+                O.ref_matmul_q8(xq, xs, xt, q, s, d, n)
+        kind, desc = "reference", "runq.c matmul_q8 (AVX-512 VNNI + OpenMP, group size 32) over the 8 shapes"
+    else:
+        cores = 1
+        n, d = SHAPES[0]
+        w = (rng.standard_normal((d, n)) * 0.02).astype(np.float32)
+        q, s = O.quantize_weight(w, GS, KIND)
+        x = rng.standard_normal(n).astype(np.float32)
+        xq, xs, _ = O.quantize_act(x, GS)
+        per = gemv_bytes(n, d, GS, KIND, 1 + 4 / GS)
+
+        def one():
+            O.gemv(xq, xs, q, s, n, GS, KIND)
+        kind, desc = "port", "scalar C oracle GEMV, one 4096x4096 INT8 GS64 matrix per step (1 thread)"
+    for _ in range(max(1, warmup)):
+        one()
+    times = []
+    t_end = time.perf_counter() + seconds
+    while (steps is None and (time.perf_counter() < t_end or not times)) or (steps is not None and len(times) < steps):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+    gbs = per * len(times) / sum(times) / 1e9
+    return gbs, kind, cores, desc + f"; {len(times)} passes", times
+
+
+# ---------------------------------------------------------------------------
+
+def setup_dist(n_gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    return rank, world, local, dist
+
+
+def run_reference(args):
+    rank, world, local, dist = setup_dist(args.gpus)
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    gbs, kind, cores, desc, times = cpu_baseline(steps=args.steps, warmup=args.warmup)
+    ms = 1e3 * sum(times) / len(times)
+    line = {"metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u8/s8 (int32 group dot, fp32 scales)", "data": "synthetic",
+            "impl": "reference",
+            "config": {"workload": WORKLOAD, "group_size_reference": 32,
+                       "note": "reference runq.c supports only group size 32 (QBLOCK, runq.c:26)"},
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+def decode_bench(lq, torch, positions: int = 2048):
+    """Config 3: Llama-2-7B-shape INT4 GS64 greedy decode from BOS over
+    positions 0..positions-1, random-init weights generated on the device."""
+    cfg = lq.Config.make(4096, 11008, 32, 32, 32, 32000, 2048)
+    t0 = time.perf_counter()
+    t = lq.Transformer.random(cfg, lq.KIND_INT4, 64, 7, positions)
+    init_s = time.perf_counter() - t0
+    token = 1
+    for pos in range(3):  # warm-up (graph capture) at the first positions
+        token = t.forward_argmax(token, pos)
+    token = 1
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for pos in range(positions):
+        token = t.forward_argmax(token, pos)
+    dt = time.perf_counter() - t0
+    t.close()
+    wbytes = (4096 * 4096 * 4 + 4096 * 11008 * 3) * 32 + 32000 * 4096
+    wbytes = wbytes // 2 + wbytes // 64 * 4
+    kv_avg = 2 * 32 * 4096 * 4 * (positions + 1) / 2
+    return {"config": "config3: llama-2-7b shape, int4 gs64, fp32 KV, greedy from BOS, batch 1",
+            "positions": positions, "tok_s": round(positions / dt, 2), "ms_per_token": round(1e3 * dt / positions, 4),
+            "weight_bytes_per_token": wbytes, "avg_kv_bytes_per_token": int(kv_avg),
+            "hbm_gbs_effective": round((wbytes + kv_avg) * positions / dt / 1e9, 1),
+            "timing": "host wall clock around forward_argmax calls (H2D token/pos, graph, D2H 4 bytes each)",
+            "init_s": round(init_s, 2)}
+
+
+def run_gpu(args):
+    import torch
+
+    rank, world, local, dist = setup_dist(args.gpus)
+    torch.cuda.set_device(local)
+    lq = importlib.import_module("llama2-min-inference_b200")
+    lq.lib()
+    stream = torch.cuda.Stream()
+    lq.set_stream(stream.cuda_stream)
+
+    keep = []
+    weights = [[None] * len(SHAPES) for _ in range(COPIES)]
+    with torch.cuda.stream(stream):
+        for c in range(COPIES):
+            for i, (n, d) in enumerate(SHAPES):
+                q = torch.empty((d, n if KIND == 8 else n // 2), dtype=torch.uint8, device="cuda")
+                s = torch.empty((d, n // GS), dtype=torch.float32, device="cuda")
+                w = lq.QuantizedTensor(q=q.data_ptr(), s=s.data_ptr(), rows=d, cols=n, group_size=GS, kind=KIND)
+                lq.synth_tensor(w, 1000 + rank, 100 * c + i, 0.02)
+                weights[c][i] = w
+                keep += [q, s]
+        gen = torch.Generator(device="cuda").manual_seed(5)
+        xs = [torch.randn(n, device="cuda", generator=gen) for n, d in SHAPES]
+        ys = [torch.empty(d, device="cuda") for n, d in SHAPES]
+    stream.synchronize()
+
+    lq.set_launch_flags(lq.LAUNCH_PDL)
+    graphs = []
+    for c in range(COPIES):
+        lq.graph_begin()
+        for i, (n, d) in enumerate(SHAPES):
+            lq.matmul_f32(ys[i].data_ptr(), xs[i].data_ptr(), weights[c][i], n, d)
+        graphs.append(lq.graph_end())
+    lq.set_launch_flags(0)
+
+    for s_ in range(args.warmup):
+        lq.graph_launch(graphs[s_ % COPIES])
+    stream.synchronize()
+    lq.sync()
+
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for s_ in range(args.steps):
+        lq.graph_launch(graphs[s_ % COPIES])
+    ev1.record(stream)
+    ev1.synchronize()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        dist.barrier()
+    clk = clocks.stop() if clocks else None
+    lq.sync()
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+
+    sb = step_bytes()
+    per_gpu_gbs = sb * args.steps / (ms / 1e3) / 1e9
+    value = per_gpu_gbs * world
+
+    # end to end through the public C ABI with pinned host buffers
+    hx = [torch.randn(n).pin_memory() for n, d in SHAPES]
+    hy = [torch.empty(d).pin_memory() for n, d in SHAPES]
+    e2e_steps = max(3, min(args.steps, 200))
+    for s_ in range(3):
+        for i, (n, d) in enumerate(SHAPES):
+            lq.matmul_f32(hy[i].data_ptr(), hx[i].data_ptr(), weights[s_ % COPIES][i], n, d)
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for s_ in range(e2e_steps):
+        for i, (n, d) in enumerate(SHAPES):
+            lq.matmul_f32(hy[i].data_ptr(), hx[i].data_ptr(), weights[s_ % COPIES][i], n, d)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_gbs = sb * e2e_steps / e2e_s / 1e9 * world
+
+    for g in graphs:
+        lq.graph_destroy(g)
+
+    extra = {}
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        gbs, kind, cores, desc, _ = cpu_baseline(seconds=args.cpu_seconds)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc}
+    if rank == 0 and world == 1 and not args.no_decode:
+        try:
+            extra["decode"] = decode_bench(lq, torch, args.decode_positions)
+        except Exception as e:  # reported, never hides the GEMV line
+            extra["decode"] = {"error": str(e)[:300]}
+
+    if rank == 0:
+        peak, peak_kind = peaks()
+        tr = traffic_per_launch()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "u8 x s8 -> int32 group dot, fp32 scales",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "group_size": GS, "weight_kind": "int8", "batch": 1,
+                       "bytes_per_step": sb, "l2": f"{COPIES} weight copies ({COPIES * sb / 1e9:.2f} GB) alternate; "
+                       "inputs larger than L2", "parallelism": f"replicas x{world}",
+                       "launch": "CUDA graph of 8 GEMV launches per step, programmatic dependent launch"},
+            "roofline": {"bound": "hbm", "achieved": round(per_gpu_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(per_gpu_gbs / peak, 4), "peak_source": peak_kind,
+                         "kernel": "lq::gemv_tma_kernel<8,1>",
+                         "traffic": (tr or {}).get("dram_bytes_per_step_scaled")},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "steps": e2e_steps,
+                    "h2d_bytes_per_step": sum(4 * n for n, d in SHAPES),
+                    "d2h_bytes_per_step": sum(4 * d for n, d in SHAPES),
+                    "path": "matmul_f32 C ABI, pinned host x and y, copies + sync inside each call"},
+            "gpu_launches": args.steps * len(SHAPES),
+            "clocks": clk,
+        }
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--decode-positions", type=int, default=2048)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

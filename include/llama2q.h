@@ -1,0 +1,192 @@
+/*
+ * llama2q — B200 (sm_100a) decode hot path of llama2-min-inference:
+ * group-quantized INT8 / INT4 weight x int8 activation GEMV with int32 group
+ * accumulation and fp32 scale epilogue, plus the decode step around it.
+ *
+ * Plain C ABI: pointers, sizes and int status codes.  No torch or C++ types.
+ * Every entry point names the reference interface it replaces (paths are
+ * relative to the reference project root).
+ *
+ * Memory: unless a function says "host or device", pointers are device
+ * pointers on the current CUDA device.  Work is issued on the stream set by
+ * lq_set_stream (default: the legacy default stream).  Functions return
+ * LQ_OK (0) or an LQ_E* code; lq_last_error() gives the message (per host
+ * thread).  The reference exits the process on every error instead
+ * (v1-int8-vnni/runq.c:258-275, v5-cuda-fused/run.cu:50-52).
+ */
+#ifndef LLAMA2Q_H
+#define LLAMA2Q_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define LQ_OK 0
+#define LQ_EINVAL 1       /* bad argument / shape / alignment */
+#define LQ_ECUDA 2        /* CUDA runtime error */
+#define LQ_ENOMEM 3       /* allocation failed */
+#define LQ_EIO 4          /* file open / read / write failed */
+#define LQ_EFORMAT 5      /* bad magic, version or truncated checkpoint */
+#define LQ_ETIMEOUT 6     /* a device-side wait ran out of its limit */
+#define LQ_EUNSUPPORTED 7 /* valid input this build does not handle */
+
+/* QuantizedTensor.kind */
+#define LQ_KIND_INT8 8    /* weights: uint8 [rows, cols] = q + 128 (quantize_int8.py:62) */
+#define LQ_KIND_INT4 4    /* weights: uint8 [rows, cols/2], two's-complement nibbles,
+                             even column in the low nibble (quantize_int4.py:47-50) */
+#define LQ_KIND_ACT8 1    /* activations: int8 [rows, cols] signed (runq.c:133) */
+
+/* Group-quantized tensor (replaces QWeight, v1-int8-vnni/runq.c:43-49, and
+ * DQWeight, v5-cuda-fused/run.cu:61-65; the activation form replaces the
+ * actq/acts pair of runq.c:85-86).  Device encodings are the checkpoint's
+ * own byte encodings, so loading a tensor is a plain copy. */
+typedef struct QuantizedTensor {
+    void* q;            /* device: quantized values (see kind) */
+    float* s;           /* device: fp32 group scales [rows, cols / group_size] */
+    int64_t rows;
+    int64_t cols;       /* multiple of group_size */
+    int32_t group_size; /* multiple of 32, <= 256 (reference: 32) */
+    int32_t kind;       /* LQ_KIND_* */
+} QuantizedTensor;
+
+/* Model hyper-parameters, v1-int8-vnni/runq.c:33-41 (same field order as
+ * the checkpoint header). vocab_size is positive here. */
+typedef struct Config {
+    int dim;
+    int hidden_dim;
+    int n_layers;
+    int n_heads;
+    int n_kv_heads;
+    int vocab_size;
+    int seq_len;
+} Config;
+
+typedef struct Transformer Transformer; /* opaque; runq.c:93-101 */
+
+/* ---- context ----------------------------------------------------------- */
+const char* lq_last_error(void);
+/* Make `device` current for this host thread; -1 picks the device with the
+ * most free memory, as the reference runners do (v2-cuda/run.cu:799-813,
+ * v5-cuda-fused/run.cu:1109-1122), and reports the choice on stderr. */
+int lq_select_device(int device);
+int lq_set_stream(void* cuda_stream); /* cudaStream_t; NULL = legacy default */
+void* lq_get_stream(void);
+/* Synchronize the stream and report any device-side error word. */
+int lq_sync(void);
+
+/* Launch flags for the operator entry points.  LQ_LAUNCH_PDL lets each
+ * operator kernel start (and start streaming its weights) while the previous
+ * kernel on the stream is still finishing — programmatic dependent launch.
+ * Activations are still read only after that kernel completes.  Set it only
+ * when no kernel queued before an operator writes that operator's weights. */
+#define LQ_LAUNCH_PDL 1
+int lq_set_launch_flags(int flags);
+
+/* Stream capture of operator calls into a CUDA graph on the library stream
+ * (the reference captures its forward the same way,
+ * v5-cuda-fused/run.cu:671-679).  lq_graph_end returns an executable graph
+ * handle for lq_graph_launch / lq_graph_destroy. */
+int lq_graph_begin(void);
+int lq_graph_end(void** graph_exec);
+int lq_graph_launch(void* graph_exec);
+void lq_graph_destroy(void* graph_exec);
+
+/* Fill a weight tensor (w->q, w->s allocated by the caller, rows/cols/
+ * group_size/kind set) with seeded synthetic values ~ N(0, std) quantized
+ * like tools/quantize_int8.py / quantize_int4.py, generated on the device;
+ * identical to quantizing lq_synth_value(seed, tensor_id, r*cols+c, std). */
+int lq_synth_tensor(QuantizedTensor* w, uint64_t seed, int tensor_id, float std);
+
+/* ---- hot-path operators -------------------------------------------------- */
+
+/* Activation quantize.  Replaces quantize_act, v1-int8-vnni/runq.c:117-139
+ * (and quantize_act_kernel, v2-cuda/run.cu:102-127): per group of
+ * out->group_size values, s = max|x|/127 (0 -> 1e-8), q = clamp(rint(x/s),
+ * +-127).  x is fp32 [out->rows, n], host or device memory; out->q (int8)
+ * and out->s must be device buffers of [rows, n] and [rows, n/gs].  Sets
+ * out->cols = n and out->kind = LQ_KIND_ACT8.  The reference's xt term is
+ * not produced: the kernels correct the weight bias from the group sums. */
+int quantize(QuantizedTensor* out, const float* x, int n);
+
+/* Quantized matrix-vector / matrix product.  Replaces matmul_q8,
+ * v1-int8-vnni/runq.c:142-159 (INT8), matmul_q4_vec_kernel,
+ * v5-cuda-fused/run.cu:276-330 (INT4) and matmul_q8_kernel,
+ * v2-cuda/run.cu:131-162 (x->rows > 1), with the signature of the fp32
+ * matmul(xout, x, w, n, d), v0-fp32/run.c:217: W (d x n) times x (n).
+ * xout[b, i] = sum_g (w.s[i,g] * x.s[b,g]) * D[b,i,g], D the exact int32
+ * group dot.  x: LQ_KIND_ACT8 [B, n]; w: LQ_KIND_INT8 / LQ_KIND_INT4 [d, n]
+ * with the same group size; xout: fp32 [B, d].  All device memory. */
+int matmul(float* xout, const QuantizedTensor* x, const QuantizedTensor* w, int n, int d);
+
+/* fp32-input form: quantize x (group size of w) inside the GEMV prologue and
+ * multiply, i.e. runq.c's quantize_act followed by matmul_q8 (runq.c:345-348)
+ * in one launch.  x fp32 [n] and xout fp32 [d] may be host or device
+ * memory; with host memory the copies are part of the call, which then
+ * returns after the result is in xout. */
+int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int d);
+
+/* ---- model ------------------------------------------------------------- */
+
+/* Load a checkpoint: QLL8 version 1 (INT8, GS 32; tools/quantize_int8.py:11-37,
+ * reader runq.c:230-278), QLL4 version 2 (INT4, GS 32; tools/quantize_int4.py:
+ * 9-26, reader v5-cuda-fused/run.cu:534-551), or version 3 of either magic,
+ * which adds an int32 group size after the config.  A positive vocab_size
+ * (shared classifier) is accepted: the fp32 embedding is quantized at load
+ * (the reference exits instead, runq.c:247-251).  max_seq_len bounds the KV
+ * cache (0 = the header's seq_len).  Replaces build_transformer,
+ * runq.c:280-283. */
+int build_transformer(Transformer** t, const char* checkpoint_path, int max_seq_len);
+
+/* Random-init model generated directly in device memory from a seed, with
+ * the same values lq_write_checkpoint_random would write (no file I/O;
+ * used for the 7B/13B/70B shapes).  kind LQ_KIND_INT8 or LQ_KIND_INT4. */
+int build_transformer_random(Transformer** t, const Config* cfg, int kind, int group_size,
+                             uint64_t seed, int max_seq_len);
+
+/* One decode step: token at absolute position pos.  Returns host logits
+ * [vocab] owned by t and overwritten by the next call, or NULL on error.
+ * Replaces forward, v1-int8-vnni/runq.c:320-421 (GPU: run_token,
+ * v5-cuda-fused/run.cu:682-695). */
+float* forward(Transformer* t, int token, int pos);
+
+/* Same step with the greedy choice made on the device: writes
+ * argmax(logits) (first index of the maximum, sample_argmax runq.c:578-585)
+ * to *next_token and copies 4 bytes instead of the logits. */
+int forward_argmax(Transformer* t, int token, int pos, int* next_token);
+
+/* Release a model (free_transformer, runq.c:285-289). */
+void free_transformer(Transformer* t);
+
+/* Copy out the model's shape, weight kind and group size. */
+int transformer_config(const Transformer* t, Config* cfg, int* kind, int* group_size);
+
+/* ---- checkpoint files (host only; no GPU needed) -------------------------- */
+
+/* Write a llama2.c fp32 checkpoint (the input format of
+ * tools/quantize_int8.py:71-96) with seeded synthetic weights: every matrix
+ * and the embedding ~ N(0, std) via the project's counter-based generator,
+ * RMSNorm weights = 1.  shared != 0 writes a positive vocab_size and no
+ * classifier. */
+int lq_write_checkpoint_fp32(const char* path, const Config* cfg, uint64_t seed, float std,
+                             int shared);
+
+/* Quantize a llama2.c fp32 checkpoint (tools/quantize_int8.py:66-126 /
+ * tools/quantize_int4.py:54-115).  group_size 32 writes the reference's own
+ * version 1 / 2 files; any other group size writes version 3. */
+int lq_quantize_checkpoint(const char* src_fp32, const char* dst, int kind, int group_size);
+
+/* Read only the header of a quantized checkpoint. */
+int lq_read_header(const char* path, Config* cfg, int* kind, int* group_size, int* shared);
+
+/* The synthetic generator used above (one value of tensor `tensor_id`,
+ * element `index`), exposed so callers can rebuild any weight exactly. */
+float lq_synth_value(uint64_t seed, int tensor_id, uint64_t index, float std);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* LLAMA2Q_H */

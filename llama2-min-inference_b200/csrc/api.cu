@@ -1,0 +1,305 @@
+// C-ABI: error reporting, stream, and the operator entry points
+// (quantize / matmul / matmul_f32).
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "lq_ctx.h"
+#include "lq_host.h"
+#include "lq_kernels.h"
+#include "lq_ops.h"
+
+namespace {
+
+thread_local char g_err[1024] = "";
+cudaStream_t g_stream = nullptr;
+int g_launch_flags = 0;
+std::mutex g_ctx_mu;
+lq::DevCtx* g_ctx[64] = {nullptr};
+
+bool is_device_ptr(const void* p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeDevice || at.type == cudaMemoryTypeManaged;
+}
+
+}  // namespace
+
+extern "C" int lq_fail(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+namespace lq {
+
+int cuda_fail(cudaError_t e, const char* what) {
+    return lq_fail(e == cudaErrorMemoryAllocation ? LQ_ENOMEM : LQ_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+DevCtx* ctx() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+    std::lock_guard<std::mutex> lk(g_ctx_mu);
+    if (!g_ctx[dev]) {
+        DevCtx* c = new DevCtx();
+        c->dev = dev;
+        if (cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaMalloc(&c->err, sizeof(int)) != cudaSuccess || cudaMemset(c->err, 0, sizeof(int)) != cudaSuccess) {
+            cudaGetLastError();
+            delete c;
+            return nullptr;
+        }
+        g_ctx[dev] = c;
+    }
+    return g_ctx[dev];
+}
+
+int ensure_scratch(DevCtx* c, size_t bytes) {
+    if (c->scratch_bytes >= bytes) return LQ_OK;
+    if (c->scratch) cudaFree(c->scratch);
+    c->scratch = nullptr;
+    c->scratch_bytes = 0;
+    cudaError_t e = cudaMalloc(&c->scratch, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "scratch allocation");
+    c->scratch_bytes = bytes;
+    return LQ_OK;
+}
+
+int check_device_error(int* err_dev, cudaStream_t st) {
+    int h = 0;
+    cudaError_t e = cudaMemcpyAsync(&h, err_dev, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "device error check");
+    if (h != 0) {
+        cudaMemsetAsync(err_dev, 0, sizeof(int), st);
+        cudaStreamSynchronize(st);
+        return lq_fail(LQ_ETIMEOUT, "device-side wait gave up (code 0x%x)", h);
+    }
+    return LQ_OK;
+}
+
+cudaStream_t stream() { return g_stream; }
+
+}  // namespace lq
+
+using namespace lq;
+
+extern "C" {
+
+const char* lq_last_error(void) { return g_err; }
+
+int lq_select_device(int device) {
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || n == 0) return lq_fail(LQ_ECUDA, "no CUDA device context (no device, or first use inside a graph capture)");
+    if (device >= n) return lq_fail(LQ_EINVAL, "device %d out of range (%d devices)", device, n);
+    if (device < 0) {
+        size_t best = 0;
+        for (int i = 0; i < n; ++i) {
+            size_t f = 0, t = 0;
+            if (cudaSetDevice(i) == cudaSuccess && cudaMemGetInfo(&f, &t) == cudaSuccess && f > best) {
+                best = f;
+                device = i;
+            }
+            cudaGetLastError();
+        }
+        if (device < 0) return lq_fail(LQ_ECUDA, "no usable CUDA device");
+    }
+    e = cudaSetDevice(device);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaSetDevice");
+    size_t f = 0, t = 0;
+    cudaMemGetInfo(&f, &t);
+    fprintf(stderr, "using GPU %d (%.1f GB free / %.1f GB)\n", device, f / 1073741824.0, t / 1073741824.0);
+    return LQ_OK;
+}
+
+int lq_set_stream(void* s) {
+    g_stream = static_cast<cudaStream_t>(s);
+    // create the device context now: its allocation is not allowed while
+    // the stream is being captured into a graph
+    if (!ctx()) return lq_fail(LQ_ECUDA, "CUDA device context could not be created");
+    return LQ_OK;
+}
+
+void* lq_get_stream(void) { return g_stream; }
+
+int lq_sync(void) {
+    DevCtx* c = ctx();
+    if (!c) return lq_fail(LQ_ECUDA, "no CUDA device context (no device, or first use inside a graph capture)");
+    return check_device_error(c->err, g_stream);
+}
+
+int lq_set_launch_flags(int flags) {
+    if (flags & ~LQ_LAUNCH_PDL) return lq_fail(LQ_EINVAL, "unknown launch flags 0x%x", flags);
+    g_launch_flags = flags;
+    return LQ_OK;
+}
+
+int lq_graph_begin(void) {
+    if (!g_stream) return lq_fail(LQ_EINVAL, "lq_graph_begin: set a non-default stream first");
+    if (!ctx()) return lq_fail(LQ_ECUDA, "CUDA device context could not be created");
+    cudaError_t e = cudaStreamBeginCapture(g_stream, cudaStreamCaptureModeThreadLocal);
+    return e == cudaSuccess ? LQ_OK : cuda_fail(e, "begin capture");
+}
+
+int lq_graph_end(void** exec) {
+    if (!exec) return lq_fail(LQ_EINVAL, "lq_graph_end: null argument");
+    cudaGraph_t g = nullptr;
+    cudaError_t e = cudaStreamEndCapture(g_stream, &g);
+    if (e != cudaSuccess) return cuda_fail(e, "end capture");
+    cudaGraphExec_t x = nullptr;
+    e = cudaGraphInstantiate(&x, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
+    *exec = x;
+    return LQ_OK;
+}
+
+int lq_graph_launch(void* exec) {
+    cudaError_t e = cudaGraphLaunch(static_cast<cudaGraphExec_t>(exec), g_stream);
+    return e == cudaSuccess ? LQ_OK : cuda_fail(e, "graph launch");
+}
+
+void lq_graph_destroy(void* exec) {
+    if (exec) cudaGraphExecDestroy(static_cast<cudaGraphExec_t>(exec));
+}
+
+int lq_synth_tensor(QuantizedTensor* w, uint64_t seed, int tensor_id, float std) {
+    if (!w || !w->q || !w->s || w->rows <= 0 || w->cols <= 0)
+        return lq_fail(LQ_EINVAL, "lq_synth_tensor: tensor not allocated");
+    if (w->kind != LQ_KIND_INT8 && w->kind != LQ_KIND_INT4) return lq_fail(LQ_EINVAL, "lq_synth_tensor: kind");
+    const int gs = w->group_size;
+    if (!(gs == 32 || gs == 64 || gs == 128 || gs == 256) || w->cols % gs)
+        return lq_fail(LQ_EINVAL, "lq_synth_tensor: group size");
+    cudaError_t e = synth_quant_launch(static_cast<uint8_t*>(w->q), w->s, w->rows, w->cols, gs, w->kind, seed,
+                                       tensor_id, std, 0, g_stream);
+    return e == cudaSuccess ? LQ_OK : cuda_fail(e, "lq_synth_tensor");
+}
+
+int quantize(QuantizedTensor* out, const float* x, int n) {
+    if (!out || !x || n <= 0) return lq_fail(LQ_EINVAL, "quantize: null argument or n <= 0");
+    const int gs = out->group_size;
+    if (gs <= 0 || gs % 32 || gs > 256 || n % gs)
+        return lq_fail(LQ_EINVAL, "quantize: n=%d must be a multiple of group_size=%d (multiple of 32, <= 256)", n, gs);
+    if (out->rows <= 0) out->rows = 1;
+    if (!out->q || !out->s) return lq_fail(LQ_EINVAL, "quantize: out->q / out->s not allocated");
+    DevCtx* c = ctx();
+    if (!c) return lq_fail(LQ_ECUDA, "no CUDA device context (no device, or first use inside a graph capture)");
+    const float* xd = x;
+    const size_t bytes = (size_t)out->rows * n * sizeof(float);
+    if (!is_device_ptr(x)) {
+        int rc = ensure_scratch(c, bytes);
+        if (rc) return rc;
+        cudaError_t e = cudaMemcpyAsync(c->scratch, x, bytes, cudaMemcpyHostToDevice, g_stream);
+        if (e != cudaSuccess) return cuda_fail(e, "quantize: copy of x");
+        xd = static_cast<const float*>(c->scratch);
+    }
+    cudaError_t e = quantize_act_launch(xd, out->rows, n, gs, static_cast<int8_t*>(out->q), out->s, g_stream);
+    if (e != cudaSuccess) return cuda_fail(e, "quantize launch");
+    if (xd != x) {
+        e = cudaStreamSynchronize(g_stream);  // the scratch copy must finish before reuse
+        if (e != cudaSuccess) return cuda_fail(e, "quantize");
+    }
+    out->cols = n;
+    out->kind = LQ_KIND_ACT8;
+    return LQ_OK;
+}
+
+static int check_weight(const QuantizedTensor* w, int n, int d, const char* fn) {
+    if (!w || !w->q || !w->s) return lq_fail(LQ_EINVAL, "%s: weight tensor not set", fn);
+    if (w->kind != LQ_KIND_INT8 && w->kind != LQ_KIND_INT4)
+        return lq_fail(LQ_EINVAL, "%s: weight kind must be LQ_KIND_INT8 or LQ_KIND_INT4", fn);
+    const int gs = w->group_size;
+    if (!(gs == 32 || gs == 64 || gs == 128 || gs == 256))
+        return lq_fail(LQ_EUNSUPPORTED, "%s: group size %d not supported (32, 64, 128, 256)", fn, gs);
+    if (n <= 0 || d <= 0 || w->cols != n || w->rows != d || n % gs)
+        return lq_fail(LQ_EINVAL, "%s: shape mismatch (w is %lld x %lld, n=%d d=%d, gs=%d)", fn,
+                       (long long)w->rows, (long long)w->cols, n, d, gs);
+    if ((reinterpret_cast<uintptr_t>(w->q) | reinterpret_cast<uintptr_t>(w->s)) & 15u)
+        return lq_fail(LQ_EINVAL, "%s: w->q and w->s must be 16-byte aligned", fn);
+    return LQ_OK;
+}
+
+int matmul(float* xout, const QuantizedTensor* x, const QuantizedTensor* w, int n, int d) {
+    int rc = check_weight(w, n, d, "matmul");
+    if (rc) return rc;
+    if (!xout || !x || !x->q || !x->s) return lq_fail(LQ_EINVAL, "matmul: null argument");
+    if (x->kind != LQ_KIND_ACT8 || x->cols != n || x->group_size != w->group_size || x->rows <= 0)
+        return lq_fail(LQ_EINVAL, "matmul: x must be an ACT8 tensor [B, n] with the weight's group size");
+    if (reinterpret_cast<uintptr_t>(x->q) & 7u) return lq_fail(LQ_EINVAL, "matmul: x->q must be 8-byte aligned");
+    DevCtx* c = ctx();
+    if (!c) return lq_fail(LQ_ECUDA, "no CUDA device context (no device, or first use inside a graph capture)");
+    const int ng = n / w->group_size;
+    int64_t done = 0;
+    while (done < x->rows) {
+        const int64_t left = x->rows - done;
+        const int nb = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;
+        GemvArgs a = {};
+        a.seg[0] = {static_cast<const uint8_t*>(w->q), w->s, xout + done * d, d, EPI_STORE};
+        a.nseg = 1;
+        a.cols = n;
+        a.gs = w->group_size;
+        a.nb = nb;
+        a.in_mode = IN_QUANT;
+        a.xq = static_cast<const int8_t*>(x->q) + done * n;
+        a.xs = x->s + done * ng;
+        a.y_stride = d;
+        a.err = c->err;
+        cudaError_t e = gemv_launch(a, w->kind, g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms);
+        if (e != cudaSuccess) return cuda_fail(e, "matmul launch");
+        done += nb;
+    }
+    return LQ_OK;
+}
+
+int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int d) {
+    int rc = check_weight(w, n, d, "matmul_f32");
+    if (rc) return rc;
+    if (!xout || !x) return lq_fail(LQ_EINVAL, "matmul_f32: null argument");
+    DevCtx* c = ctx();
+    if (!c) return lq_fail(LQ_ECUDA, "no CUDA device context (no device, or first use inside a graph capture)");
+    const bool xdev = is_device_ptr(x), ydev = is_device_ptr(xout);
+    const float* xd = x;
+    float* yd = xout;
+    if (!xdev || !ydev) {
+        const size_t xb = ((size_t)n * 4 + 255) / 256 * 256;
+        rc = ensure_scratch(c, xb + (size_t)d * 4);
+        if (rc) return rc;
+        if (!xdev) {
+            cudaError_t e = cudaMemcpyAsync(c->scratch, x, (size_t)n * 4, cudaMemcpyHostToDevice, g_stream);
+            if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of x");
+            xd = static_cast<const float*>(c->scratch);
+        }
+        if (!ydev) yd = reinterpret_cast<float*>(static_cast<char*>(c->scratch) + xb);
+    }
+    GemvArgs a = {};
+    a.seg[0] = {static_cast<const uint8_t*>(w->q), w->s, yd, d, EPI_STORE};
+    a.nseg = 1;
+    a.cols = n;
+    a.gs = w->group_size;
+    a.nb = 1;
+    a.in_mode = IN_F32;
+    a.xf = xd;
+    a.y_stride = d;
+    a.err = c->err;
+    cudaError_t e = gemv_launch(a, w->kind, g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms);
+    if (e != cudaSuccess) return cuda_fail(e, "matmul_f32 launch");
+    if (!xdev || !ydev) {
+        if (!ydev) {
+            e = cudaMemcpyAsync(xout, yd, (size_t)d * 4, cudaMemcpyDeviceToHost, g_stream);
+            if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of xout");
+        }
+        e = cudaStreamSynchronize(g_stream);
+        if (e != cudaSuccess) return cuda_fail(e, "matmul_f32");
+    }
+    return LQ_OK;
+}
+
+}  // extern "C"

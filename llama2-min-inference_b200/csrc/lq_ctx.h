@@ -1,0 +1,22 @@
+// Per-device context shared by the C-ABI sources (C++ only).
+#pragma once
+#include <cstddef>
+#include <cuda_runtime.h>
+
+namespace lq {
+
+struct DevCtx {
+    int dev = 0;
+    int num_sms = 148;
+    int* err = nullptr;         // device error word for stand-alone operator calls
+    void* scratch = nullptr;    // staging for host-pointer calls
+    size_t scratch_bytes = 0;
+};
+
+DevCtx* ctx();  // context of the current device (created on first use)
+int ensure_scratch(DevCtx* c, size_t bytes);
+int cuda_fail(cudaError_t e, const char* what);
+int check_device_error(int* err_dev, cudaStream_t st);
+cudaStream_t stream();
+
+}  // namespace lq

@@ -1,0 +1,81 @@
+// Kernel argument blocks and launchers (host-visible, C++ only).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace lq {
+
+// What the GEMV does with a finished row value v (per segment).
+enum Epilogue : int {
+    EPI_STORE = 0,        // y[r] = v
+    EPI_ADD = 1,          // y[r] += v            (residual stream)
+    EPI_ROPE_Q = 2,       // rotary pair (r, r+1) of the query, stored to y
+    EPI_ROPE_KCACHE = 3,  // rotary pair of the key, stored to the K cache at pos
+    EPI_VCACHE = 4,       // value stored to the V cache at pos
+    EPI_SWIGLU = 5,       // paired tensors: y[r] = silu(v1) * v3 (runq.c:405-410)
+};
+
+// Where the int8 activation comes from (the GEMV prologue builds it in
+// shared memory; every CTA computes the identical quantization).
+enum InputMode : int {
+    IN_QUANT = 0,        // pre-quantized xq/xs (the C-ABI matmul)
+    IN_F32 = 1,          // fp32 x, quantized in the prologue
+    IN_RMSNORM = 2,      // rmsnorm(x) * w, then quantized
+    IN_RMSNORM_EMB = 3,  // x = emb[token] (CTA 0 also writes it to x_out), then as IN_RMSNORM
+};
+
+struct GemvSeg {
+    const uint8_t* wq;  // packed weights [rows, row_bytes]
+    const float* ws;    // group scales [rows, cols / gs]
+    float* y;           // destination (meaning depends on epi)
+    int rows;
+    int epi;
+    const uint8_t* wq2;  // EPI_SWIGLU: the second tensor (w3), same shape
+    const float* ws2;
+};
+
+constexpr int kMaxSegs = 3;
+constexpr int kConsumerWarps = 8;
+constexpr int kGemvThreads = kConsumerWarps * 32;
+
+struct GemvArgs {
+    GemvSeg seg[kMaxSegs];
+    int nseg;
+    int cols;        // n (input length)
+    int gs;          // group size: 32, 64, 128 or 256
+    int nb;          // activation rows (batch); template NB must equal it
+    // input
+    int in_mode;
+    const int8_t* xq;  // IN_QUANT [nb, cols]
+    const float* xs;   // IN_QUANT [nb, cols/gs]
+    const float* xf;   // fp32 source [nb, cols] (IN_F32, IN_RMSNORM)
+    const float* rms_w;
+    const float* emb;  // IN_RMSNORM_EMB table [vocab, cols]
+    float* x_out;      // IN_RMSNORM_EMB residual stream init
+    int y_stride;      // elements between batch rows of y (EPI_STORE / EPI_ADD)
+    // decode state
+    const int* meta;   // per batch row: [token, pos]
+    int head_size;
+    float* kcache;     // layer base, [kv_heads][max_seq][head_size] per sequence
+    float* vcache;
+    int max_seq;
+    int64_t kv_seq_stride;  // elements between sequences' caches
+    int* err;
+    // schedule (filled by the planner)
+    int split;       // 0: stages of whole rows; 1: stages are slices of one row
+    int stage_rows;  // rows per stage (whole-row mode)
+    int slice_bytes; // slice size (slice mode)
+    int nstages;
+    int wcap, scap;  // per-stage weight / scale capacity in bytes (both tensors when paired)
+    int x_bytes;     // shared-memory bytes for the staged activation
+    int paired;      // segments carry a second tensor (EPI_SWIGLU)
+};
+
+// Plan and launch.  pdl: allow programmatic dependent launch overlap with
+// the previous kernel on the stream.  Returns a cudaError_t.
+cudaError_t gemv_launch(GemvArgs a, int kind, cudaStream_t st, bool pdl, int num_sms);
+
+// True when the kernel accepts these shapes/pointers.
+bool gemv_args_ok(const GemvArgs& a, int kind);
+
+}  // namespace lq

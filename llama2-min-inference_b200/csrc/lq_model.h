@@ -1,0 +1,47 @@
+// Transformer state (C++ only; opaque in the C ABI).
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "lq_host.h"
+
+namespace lq {
+
+struct QW {
+    uint8_t* q = nullptr;  // device, stacked over layers [L*rows, row_bytes]
+    float* s = nullptr;    // device, [L*rows, cols/gs]
+    int64_t rows = 0, cols = 0;
+};
+
+int forward_launch(Transformer* t, int batch);
+int run_step(Transformer* t, const int* tokens, const int* pos, int batch, bool want_logits, bool want_next);
+int kernels_per_step(const Transformer* t);
+
+}  // namespace lq
+
+struct Transformer {
+    Config c{};
+    int kind = 0, gs = 0, shared = 0;
+    int dev = 0, num_sms = 148;
+    int max_seq = 0, max_batch = 1;
+    int head_size = 0, kv_dim = 0, kv_mul = 1, max_splits = 1;
+    cudaStream_t stream = nullptr;
+    // weights
+    float *emb = nullptr, *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr;
+    lq::QW wq, wk, wv, wo, w1, w2, w3, wcls;
+    // activations and caches (device); leading dimension max_batch
+    float *x = nullptr, *q = nullptr, *att = nullptr, *h1 = nullptr, *h3 = nullptr, *logits = nullptr;
+    float *kc = nullptr, *vc = nullptr;  // [B][L][kv_heads][max_seq][head_size]
+    float* part = nullptr;               // attention partials
+    int* counters = nullptr;             // attention arrival counters
+    int* meta = nullptr;                 // [B][token, pos]
+    int* next = nullptr;                 // [B] argmax
+    int* err = nullptr;                  // device error word
+    // pinned host mirrors
+    float* h_logits = nullptr;
+    int *h_meta = nullptr, *h_next = nullptr, *h_err = nullptr;
+    // graph
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    int graph_batch = 0;
+};

@@ -1,0 +1,36 @@
+// Launchers for the non-GEMV kernels (host-visible, C++ only).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace lq {
+
+constexpr int kChunk = 64;         // attention positions per CTA
+constexpr int kAttnThreads = 256;
+
+struct AttnArgs {
+    const float* q;      // [batch][q_stride], query heads already rotated
+    const float* kcache; // layer base; [kv_heads][max_seq][head_size] per sequence
+    const float* vcache;
+    float* out;          // [batch][q_stride] normalised attention output
+    float* part;         // [batch][n_heads][max_splits][head_size + 2] partials
+    int* counters;       // [batch][n_kv_heads], zero between steps
+    const int* meta;     // [batch][token, pos]
+    int64_t kv_seq_stride;
+    int q_stride;
+    int n_heads, n_kv_heads, kv_mul, head_size, max_seq, max_splits;
+};
+
+cudaError_t quantize_act_launch(const float* x, int64_t rows, int64_t n, int gs, int8_t* xq, float* xs,
+                                cudaStream_t st);
+size_t attention_smem_bytes(int head_size, int kv_mul);
+cudaError_t attention_launch(const AttnArgs& a, int batch, cudaStream_t st, bool pdl);
+cudaError_t argmax_launch(const float* logits, int n, int batch, int stride, int* out, cudaStream_t st,
+                          bool pdl);
+cudaError_t synth_f32_launch(float* out, int64_t n, uint64_t seed, int tid, float std, int ones,
+                             cudaStream_t st);
+cudaError_t synth_quant_launch(uint8_t* q, float* s, int64_t rows, int64_t cols, int gs, int kind,
+                               uint64_t seed, int tid, float std, int64_t row0, cudaStream_t st);
+
+}  // namespace lq

@@ -1,0 +1,469 @@
+// Transformer: checkpoint upload / on-device random init, and the decode
+// step captured as one CUDA graph.
+//
+// Per layer the step is five kernels (reference order, runq.c:335-415):
+//   1. GEMV [wq|wk|wv]   prologue rmsnorm(x)+quantize (layer 0: x = emb[token])
+//                        epilogue RoPE(q) -> q, RoPE(k) -> K cache, v -> V cache
+//   2. attention         split-KV over the cache, normalised fp32 output
+//   3. GEMV wo           prologue quantize(att), epilogue x += .
+//   4. GEMV [w1|w3]      prologue rmsnorm(x)+quantize, epilogue h = silu(w1 x) * (w3 x)
+//   5. GEMV w2           prologue quantize(h), epilogue x += .
+// then GEMV wcls (prologue final rmsnorm + quantize) and argmax.  Every
+// kernel is launched with programmatic dependent launch, so each GEMV's
+// weight stream starts while its predecessor is finishing.  The graph reads
+// token and position from device memory (the reference's d_meta idea,
+// v5-cuda-fused/run.cu:671-695), so one graph serves every step.
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "lq_ctx.h"
+#include "lq_host.h"
+#include "lq_kernels.h"
+#include "lq_model.h"
+#include "lq_ops.h"
+
+using namespace lq;
+
+namespace {
+
+int64_t rbytes(int64_t cols, int kind) { return kind == LQ_KIND_INT8 ? cols : cols / 2; }
+
+int alloc_q(QW& w, int64_t rows, int64_t cols, int gs, int kind) {
+    w.rows = rows;
+    w.cols = cols;
+    cudaError_t e = cudaMalloc(&w.q, (size_t)(rows * rbytes(cols, kind)));
+    if (e == cudaSuccess) e = cudaMalloc(&w.s, (size_t)(rows * (cols / gs) * 4));
+    return e == cudaSuccess ? LQ_OK : cuda_fail(e, "weight allocation");
+}
+
+template <typename T>
+int dalloc(T** p, size_t count) {
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T));
+    if (e != cudaSuccess) return cuda_fail(e, "device allocation");
+    return LQ_OK;
+}
+
+QW* weight_by_id(Transformer* t, int id) {
+    switch (id) {
+        case LQ_T_WQ: return &t->wq;
+        case LQ_T_WK: return &t->wk;
+        case LQ_T_WV: return &t->wv;
+        case LQ_T_WO: return &t->wo;
+        case LQ_T_W1: return &t->w1;
+        case LQ_T_W2: return &t->w2;
+        case LQ_T_W3: return &t->w3;
+        case LQ_T_WCLS: return &t->wcls;
+    }
+    return nullptr;
+}
+
+float** f32_by_id(Transformer* t, int id) {
+    switch (id) {
+        case LQ_T_EMB: return &t->emb;
+        case LQ_T_RMS_ATT: return &t->rms_att;
+        case LQ_T_RMS_FFN: return &t->rms_ffn;
+        case LQ_T_RMS_FINAL: return &t->rms_final;
+    }
+    return nullptr;
+}
+
+int check_config(const Config* c, int gs) {
+    LqTensorDesc t[LQ_NT];
+    if (lq_tensor_table(c, t) != LQ_OK) return lq_fail(LQ_EINVAL, "bad model config");
+    const int hs = c->dim / c->n_heads;
+    if (hs % 2 || hs % 4) return lq_fail(LQ_EUNSUPPORTED, "head size %d must be a multiple of 4", hs);
+    if (c->dim % gs || c->hidden_dim % gs) return lq_fail(LQ_EINVAL, "dim and hidden_dim must be multiples of gs");
+    return LQ_OK;
+}
+
+// device state sized for max_batch sequences
+int alloc_state(Transformer* t) {
+    const Config& c = t->c;
+    const int B = t->max_batch;
+    t->head_size = c.dim / c.n_heads;
+    t->kv_dim = c.dim * c.n_kv_heads / c.n_heads;
+    t->kv_mul = c.n_heads / c.n_kv_heads;
+    t->max_splits = (t->max_seq + kChunk - 1) / kChunk;
+    const size_t kv = (size_t)B * c.n_layers * t->kv_dim * t->max_seq;
+    int rc = LQ_OK;
+    rc = rc ? rc : dalloc(&t->x, (size_t)B * c.dim);
+    rc = rc ? rc : dalloc(&t->q, (size_t)B * c.dim);
+    rc = rc ? rc : dalloc(&t->att, (size_t)B * c.dim);
+    rc = rc ? rc : dalloc(&t->h1, (size_t)B * c.hidden_dim);
+    rc = rc ? rc : dalloc(&t->h3, (size_t)B * c.hidden_dim);
+    rc = rc ? rc : dalloc(&t->logits, (size_t)B * c.vocab_size);
+    rc = rc ? rc : dalloc(&t->kc, kv);
+    rc = rc ? rc : dalloc(&t->vc, kv);
+    rc = rc ? rc : dalloc(&t->part, (size_t)B * c.n_heads * t->max_splits * (t->head_size + 2));
+    rc = rc ? rc : dalloc(&t->counters, (size_t)B * c.n_kv_heads);
+    rc = rc ? rc : dalloc(&t->meta, (size_t)2 * B);
+    rc = rc ? rc : dalloc(&t->next, (size_t)B);
+    rc = rc ? rc : dalloc(&t->err, 1);
+    if (rc) return rc;
+    cudaError_t e = cudaMemset(t->counters, 0, (size_t)B * c.n_kv_heads * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(t->err, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(t->meta, 0, 2 * B * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(t->kc, 0, kv * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(t->vc, 0, kv * sizeof(float));
+    if (e == cudaSuccess) e = cudaMallocHost(&t->h_logits, (size_t)B * c.vocab_size * sizeof(float));
+    if (e == cudaSuccess) e = cudaMallocHost(&t->h_meta, 2 * B * sizeof(int) + 64);
+    if (e == cudaSuccess) e = cudaMallocHost(&t->h_next, B * sizeof(int) + 64);
+    if (e == cudaSuccess) e = cudaMallocHost(&t->h_err, 64);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&t->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) return cuda_fail(e, "state allocation");
+    return LQ_OK;
+}
+
+Transformer* new_transformer(const Config* c, int kind, int gs, int max_seq, int max_batch) {
+    Transformer* t = new Transformer();
+    t->c = *c;
+    t->kind = kind;
+    t->gs = gs;
+    t->max_seq = (max_seq > 0 && max_seq < c->seq_len) ? max_seq : c->seq_len;
+    t->max_batch = max_batch;
+    cudaGetDevice(&t->dev);
+    cudaDeviceGetAttribute(&t->num_sms, cudaDevAttrMultiProcessorCount, t->dev);
+    return t;
+}
+
+}  // namespace
+
+namespace lq {
+
+// Issue one decode step for `batch` sequences on t->stream (capturable).
+int forward_launch(Transformer* t, int batch) {
+    const Config& c = t->c;
+    const int kind = t->kind, gs = t->gs;
+    const int D = c.dim, H = c.hidden_dim, KV = t->kv_dim, hs = t->head_size;
+    const int64_t rbD = rbytes(D, kind), rbH = rbytes(H, kind);
+    const int ngD = D / gs, ngH = H / gs;
+    const int64_t kv_layer = (int64_t)c.n_kv_heads * t->max_seq * hs;
+    const int64_t kv_seq = (int64_t)c.n_layers * kv_layer;
+    cudaStream_t st = t->stream;
+    auto base = [&](GemvArgs& a, int cols) {
+        a = GemvArgs{};
+        a.cols = cols;
+        a.gs = gs;
+        a.nb = batch;
+        a.y_stride = D;
+        a.meta = t->meta;
+        a.head_size = hs;
+        a.max_seq = t->max_seq;
+        a.kv_seq_stride = kv_seq;
+        a.err = t->err;
+    };
+    cudaError_t e;
+    for (int l = 0; l < c.n_layers; ++l) {
+        GemvArgs a;
+        // 1. q, k, v
+        base(a, D);
+        a.seg[0] = {t->wq.q + (size_t)l * D * rbD, t->wq.s + (size_t)l * D * ngD, t->q, D, EPI_ROPE_Q};
+        a.seg[1] = {t->wk.q + (size_t)l * KV * rbD, t->wk.s + (size_t)l * KV * ngD, nullptr, KV, EPI_ROPE_KCACHE};
+        a.seg[2] = {t->wv.q + (size_t)l * KV * rbD, t->wv.s + (size_t)l * KV * ngD, nullptr, KV, EPI_VCACHE};
+        a.nseg = 3;
+        a.in_mode = l == 0 ? IN_RMSNORM_EMB : IN_RMSNORM;
+        a.xf = t->x;
+        a.rms_w = t->rms_att + (size_t)l * D;
+        a.emb = t->emb;
+        a.x_out = t->x;
+        a.kcache = t->kc + l * kv_layer;
+        a.vcache = t->vc + l * kv_layer;
+        if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
+        // 2. attention
+        AttnArgs at{};
+        at.q = t->q;
+        at.kcache = t->kc + l * kv_layer;
+        at.vcache = t->vc + l * kv_layer;
+        at.out = t->att;
+        at.part = t->part;
+        at.counters = t->counters;
+        at.meta = t->meta;
+        at.kv_seq_stride = kv_seq;
+        at.q_stride = D;
+        at.n_heads = c.n_heads;
+        at.n_kv_heads = c.n_kv_heads;
+        at.kv_mul = t->kv_mul;
+        at.head_size = hs;
+        at.max_seq = t->max_seq;
+        at.max_splits = t->max_splits;
+        if ((e = attention_launch(at, batch, st, true)) != cudaSuccess) return cuda_fail(e, "attention");
+        // 3. wo + residual
+        base(a, D);
+        a.seg[0] = {t->wo.q + (size_t)l * D * rbD, t->wo.s + (size_t)l * D * ngD, t->x, D, EPI_ADD};
+        a.nseg = 1;
+        a.in_mode = IN_F32;
+        a.xf = t->att;
+        if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "wo gemv");
+        // 4. w1 | w3 paired, SwiGLU in the epilogue: h1 = silu(x.w1) * (x.w3)
+        base(a, D);
+        a.seg[0] = {t->w1.q + (size_t)l * H * rbD, t->w1.s + (size_t)l * H * ngD, t->h1, H, EPI_SWIGLU,
+                    t->w3.q + (size_t)l * H * rbD, t->w3.s + (size_t)l * H * ngD};
+        a.nseg = 1;
+        a.paired = 1;
+        a.y_stride = H;
+        a.in_mode = IN_RMSNORM;
+        a.xf = t->x;
+        a.rms_w = t->rms_ffn + (size_t)l * D;
+        if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w1/w3 gemv");
+        // 5. w2 + residual
+        base(a, H);
+        a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->x, D, EPI_ADD};
+        a.nseg = 1;
+        a.in_mode = IN_F32;
+        a.xf = t->h1;
+        if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
+    }
+    GemvArgs a;
+    base(a, D);
+    a.seg[0] = {t->wcls.q, t->wcls.s, t->logits, c.vocab_size, EPI_STORE};
+    a.nseg = 1;
+    a.y_stride = c.vocab_size;
+    a.in_mode = IN_RMSNORM;
+    a.xf = t->x;
+    a.rms_w = t->rms_final;
+    if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "classifier gemv");
+    if ((e = argmax_launch(t->logits, c.vocab_size, batch, c.vocab_size, t->next, st, true)) != cudaSuccess)
+        return cuda_fail(e, "argmax");
+    return LQ_OK;
+}
+
+int kernels_per_step(const Transformer* t) { return 5 * t->c.n_layers + 2; }
+
+static int ensure_graph(Transformer* t, int batch) {
+    if (t->exec && t->graph_batch == batch) return LQ_OK;
+    if (t->exec) {
+        cudaGraphExecDestroy(t->exec);
+        t->exec = nullptr;
+    }
+    if (t->graph) {
+        cudaGraphDestroy(t->graph);
+        t->graph = nullptr;
+    }
+    cudaError_t e = cudaStreamBeginCapture(t->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return cuda_fail(e, "begin capture");
+    int rc = forward_launch(t, batch);
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(t->stream, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "end capture");
+    t->graph = g;
+    e = cudaGraphInstantiate(&t->exec, g, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
+    t->graph_batch = batch;
+    return LQ_OK;
+}
+
+// One step for `batch` sequences: H2D tokens/positions, graph, optional D2H.
+int run_step(Transformer* t, const int* tokens, const int* pos, int batch, bool want_logits, bool want_next) {
+    if (batch < 1 || batch > t->max_batch) return lq_fail(LQ_EINVAL, "batch %d out of range", batch);
+    for (int b = 0; b < batch; ++b) {
+        if (tokens[b] < 0 || tokens[b] >= t->c.vocab_size)
+            return lq_fail(LQ_EINVAL, "token %d out of range [0, %d)", tokens[b], t->c.vocab_size);
+        if (pos[b] < 0 || pos[b] >= t->max_seq)
+            return lq_fail(LQ_EINVAL, "pos %d out of range [0, %d)", pos[b], t->max_seq);
+        t->h_meta[2 * b] = tokens[b];
+        t->h_meta[2 * b + 1] = pos[b];
+    }
+    int rc = ensure_graph(t, batch);
+    if (rc) return rc;
+    cudaStream_t st = t->stream;
+    cudaError_t e = cudaMemcpyAsync(t->meta, t->h_meta, 2 * batch * sizeof(int), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaGraphLaunch(t->exec, st);
+    if (e == cudaSuccess && want_logits)
+        e = cudaMemcpyAsync(t->h_logits, t->logits, (size_t)batch * t->c.vocab_size * sizeof(float),
+                            cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && want_next)
+        e = cudaMemcpyAsync(t->h_next, t->next, batch * sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(t->h_err, t->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_fail(e, "decode step");
+    if (t->h_err[0] != 0) {
+        const int code = t->h_err[0];
+        cudaMemsetAsync(t->err, 0, sizeof(int), st);
+        cudaStreamSynchronize(st);
+        return lq_fail(LQ_ETIMEOUT, "device-side wait gave up in the decode step (code 0x%x)", code);
+    }
+    return LQ_OK;
+}
+
+}  // namespace lq
+
+extern "C" {
+
+int build_transformer(Transformer** out, const char* path, int max_seq_len) {
+    if (!out || !path) return lq_fail(LQ_EINVAL, "build_transformer: null argument");
+    *out = nullptr;
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) return lq_fail(LQ_EIO, "couldn't open file %s", path);
+    struct stat st;
+    fstat(fd, &st);
+    const size_t size = (size_t)st.st_size;
+    const uint8_t* data = size ? (const uint8_t*)mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0)
+                               : (const uint8_t*)MAP_FAILED;
+    close(fd);
+    if (data == MAP_FAILED) return lq_fail(LQ_EIO, "mmap failed: %s", path);
+    Config c;
+    int kind, gs, shared;
+    size_t hb;
+    int rc = lq_parse_header(data, size, &c, &kind, &gs, &shared, &hb);
+    if (!rc) rc = check_config(&c, gs);
+    LqTensorDesc td[LQ_NT];
+    if (!rc) rc = lq_tensor_table(&c, td);
+    // size check (the reference does none: runq.c:269-277)
+    if (!rc) {
+        size_t need = hb;
+        for (int i = 0; i < LQ_NT; ++i) {
+            if (td[i].id == LQ_T_WCLS && shared) break;
+            need += td[i].quantized ? (size_t)lq_qtensor_bytes(td[i].rows, td[i].cols, gs, kind)
+                                    : (size_t)(td[i].rows * td[i].cols * 4);
+        }
+        if (need > size) rc = lq_fail(LQ_EFORMAT, "truncated checkpoint: %zu bytes, need %zu", size, need);
+    }
+    Transformer* t = nullptr;
+    if (!rc) {
+        t = new_transformer(&c, kind, gs, max_seq_len, 1);
+        t->shared = shared;
+        const uint8_t* p = data + hb;
+        for (int i = 0; i < LQ_NT && !rc; ++i) {
+            const LqTensorDesc& d = td[i];
+            cudaError_t e = cudaSuccess;
+            if (d.id == LQ_T_WCLS && shared) {
+                // extension: quantize the fp32 embedding as the classifier
+                rc = alloc_q(t->wcls, d.rows, d.cols, gs, kind);
+                if (rc) break;
+                std::vector<uint8_t> q((size_t)(d.rows * rbytes(d.cols, kind)));
+                std::vector<float> s((size_t)(d.rows * (d.cols / gs)));
+                std::vector<float> emb((size_t)(d.rows * d.cols));
+                cudaMemcpy(emb.data(), t->emb, emb.size() * 4, cudaMemcpyDeviceToHost);
+                lq_quantize_rows_host(emb.data(), d.rows, d.cols, gs, kind, q.data(), s.data());
+                e = cudaMemcpy(t->wcls.q, q.data(), q.size(), cudaMemcpyHostToDevice);
+                if (e == cudaSuccess) e = cudaMemcpy(t->wcls.s, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
+            } else if (d.quantized) {
+                QW* w = weight_by_id(t, d.id);
+                rc = alloc_q(*w, d.rows, d.cols, gs, kind);
+                if (rc) break;
+                const size_t qb = (size_t)(d.rows * rbytes(d.cols, kind)), sb = (size_t)(d.rows * (d.cols / gs) * 4);
+                e = cudaMemcpy(w->q, p, qb, cudaMemcpyHostToDevice);
+                if (e == cudaSuccess) e = cudaMemcpy(w->s, p + qb, sb, cudaMemcpyHostToDevice);
+                p += qb + sb;
+            } else {
+                float** f = f32_by_id(t, d.id);
+                const size_t n = (size_t)(d.rows * d.cols);
+                rc = dalloc(f, n);
+                if (rc) break;
+                e = cudaMemcpy(*f, p, n * 4, cudaMemcpyHostToDevice);
+                p += n * 4;
+            }
+            if (!rc && e != cudaSuccess) rc = cuda_fail(e, "weight upload");
+        }
+        if (!rc) rc = alloc_state(t);
+    }
+    munmap((void*)data, size);
+    if (rc) {
+        if (t) free_transformer(t);
+        return rc;
+    }
+    *out = t;
+    return LQ_OK;
+}
+
+int build_transformer_random(Transformer** out, const Config* cfg, int kind, int gs, uint64_t seed,
+                             int max_seq_len) {
+    if (!out || !cfg) return lq_fail(LQ_EINVAL, "build_transformer_random: null argument");
+    *out = nullptr;
+    if (kind != LQ_KIND_INT8 && kind != LQ_KIND_INT4) return lq_fail(LQ_EINVAL, "kind must be INT8 or INT4");
+    if (!(gs == 32 || gs == 64 || gs == 128 || gs == 256)) return lq_fail(LQ_EUNSUPPORTED, "group size %d", gs);
+    int rc = check_config(cfg, gs);
+    if (rc) return rc;
+    LqTensorDesc td[LQ_NT];
+    lq_tensor_table(cfg, td);
+    Transformer* t = new_transformer(cfg, kind, gs, max_seq_len, 1);
+    const float std = 0.02f;
+    for (int i = 0; i < LQ_NT && !rc; ++i) {
+        const LqTensorDesc& d = td[i];
+        cudaError_t e;
+        if (d.quantized) {
+            QW* w = weight_by_id(t, d.id);
+            rc = alloc_q(*w, d.rows, d.cols, gs, kind);
+            if (rc) break;
+            e = synth_quant_launch(w->q, w->s, d.rows, d.cols, gs, kind, seed, d.id, std, 0, nullptr);
+        } else {
+            float** f = f32_by_id(t, d.id);
+            const int64_t n = d.rows * d.cols;
+            rc = dalloc(f, (size_t)n);
+            if (rc) break;
+            const int ones = d.id != LQ_T_EMB;
+            e = synth_f32_launch(*f, n, seed, d.id, std, ones, nullptr);
+        }
+        if (e != cudaSuccess) rc = cuda_fail(e, "random init");
+    }
+    if (!rc) {
+        cudaError_t e = cudaDeviceSynchronize();
+        if (e != cudaSuccess) rc = cuda_fail(e, "random init");
+    }
+    if (!rc) rc = alloc_state(t);
+    if (rc) {
+        free_transformer(t);
+        return rc;
+    }
+    *out = t;
+    return LQ_OK;
+}
+
+float* forward(Transformer* t, int token, int pos) {
+    if (!t) {
+        lq_fail(LQ_EINVAL, "forward: null transformer");
+        return nullptr;
+    }
+    if (run_step(t, &token, &pos, 1, true, false) != LQ_OK) return nullptr;
+    return t->h_logits;
+}
+
+int forward_argmax(Transformer* t, int token, int pos, int* next_token) {
+    if (!t || !next_token) return lq_fail(LQ_EINVAL, "forward_argmax: null argument");
+    int rc = run_step(t, &token, &pos, 1, false, true);
+    if (rc) return rc;
+    *next_token = t->h_next[0];
+    return LQ_OK;
+}
+
+void free_transformer(Transformer* t) {
+    if (!t) return;
+    if (t->stream) cudaStreamSynchronize(t->stream);
+    if (t->exec) cudaGraphExecDestroy(t->exec);
+    if (t->graph) cudaGraphDestroy(t->graph);
+    QW* ws[] = {&t->wq, &t->wk, &t->wv, &t->wo, &t->w1, &t->w2, &t->w3, &t->wcls};
+    for (QW* w : ws) {
+        cudaFree(w->q);
+        cudaFree(w->s);
+    }
+    void* bufs[] = {t->emb, t->rms_att, t->rms_ffn, t->rms_final, t->x, t->q, t->att, t->h1, t->h3,
+                    t->logits, t->kc, t->vc, t->part, t->counters, t->meta, t->next, t->err};
+    for (void* b : bufs) cudaFree(b);
+    cudaFreeHost(t->h_logits);
+    cudaFreeHost(t->h_meta);
+    cudaFreeHost(t->h_next);
+    cudaFreeHost(t->h_err);
+    if (t->stream) cudaStreamDestroy(t->stream);
+    delete t;
+}
+
+int transformer_config(const Transformer* t, Config* cfg, int* kind, int* group_size) {
+    if (!t) return lq_fail(LQ_EINVAL, "transformer_config: null transformer");
+    if (cfg) *cfg = t->c;
+    if (kind) *kind = t->kind;
+    if (group_size) *group_size = t->gs;
+    return LQ_OK;
+}
+
+}  // extern "C"

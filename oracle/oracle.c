@@ -1,0 +1,400 @@
+/*
+ * Scalar CPU oracle for the group-quantized decode hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY: loaded by tests/, __graft_entry__.smoke() and the
+ * CPU-baseline leg of bench.py, never by the product library.
+ *
+ * Each function cites the reference lines it restates (paths relative to the
+ * reference project root).  The group size is a parameter; at GS=32 the INT8
+ * path is pinned against runq.c itself (tests/test_oracle_pin.py and the
+ * fixtures in tests/golden/).
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------------ */
+/* activation quantize: v1-int8-vnni/runq.c:117-139                         */
+
+void orc_quantize_act(const float* x, int n, int gs, int8_t* xq, float* xs, float* xt) {
+    int nb = n / gs;
+    for (int b = 0; b < nb; b++) {
+        const float* xb = x + (size_t)b * gs;
+        float amax = 0.0f;
+        for (int j = 0; j < gs; j++) {
+            float a = fabsf(xb[j]);
+            if (a > amax) amax = a;
+        }
+        float s = amax / 127.0f;
+        if (s == 0.0f) s = 1e-8f;
+        int sum = 0;
+        for (int j = 0; j < gs; j++) {
+            int q = (int)lrintf(xb[j] / s);
+            if (q > 127) q = 127;
+            if (q < -127) q = -127;
+            xq[(size_t)b * gs + j] = (int8_t)q;
+            sum += q;
+        }
+        xs[b] = s;
+        if (xt) xt[b] = s * 128.0f * (float)sum;
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* weight quantizers: tools/quantize_int8.py:52-63, tools/quantize_int4.py:38-51
+ * numpy float32 arithmetic: amax / 127.0 stays float32 (NEP 50), the division
+ * w / scale is float32, np.rint rounds half to even (rintf in the default
+ * rounding mode).                                                           */
+
+static float group_scale(const float* w, int gs, float qmax) {
+    float amax = 0.0f;
+    for (int j = 0; j < gs; j++) {
+        float a = fabsf(w[j]);
+        if (a > amax) amax = a;
+    }
+    float s = amax / qmax;
+    if (s == 0.0f) s = 1e-8f;
+    return s;
+}
+
+void orc_quantize_w8(const float* w, int64_t rows, int64_t cols, int gs, uint8_t* q, float* s) {
+    int64_t ng = cols / gs;
+    for (int64_t r = 0; r < rows; r++) {
+        for (int64_t g = 0; g < ng; g++) {
+            const float* wg = w + r * cols + g * gs;
+            float sc = group_scale(wg, gs, 127.0f);
+            s[r * ng + g] = sc;
+            for (int j = 0; j < gs; j++) {
+                float v = rintf(wg[j] / sc);
+                if (v > 127.0f) v = 127.0f;
+                if (v < -127.0f) v = -127.0f;
+                q[r * cols + g * gs + j] = (uint8_t)(int)(v + 128.0f);
+            }
+        }
+    }
+}
+
+void orc_quantize_w4(const float* w, int64_t rows, int64_t cols, int gs, uint8_t* q, float* s) {
+    int64_t ng = cols / gs;
+    for (int64_t r = 0; r < rows; r++) {
+        for (int64_t g = 0; g < ng; g++) {
+            const float* wg = w + r * cols + g * gs;
+            float sc = group_scale(wg, gs, 8.0f);
+            s[r * ng + g] = sc;
+            for (int j = 0; j < gs; j += 2) {
+                float v0 = rintf(wg[j] / sc), v1 = rintf(wg[j + 1] / sc);
+                if (v0 > 7.0f) v0 = 7.0f;
+                if (v0 < -8.0f) v0 = -8.0f;
+                if (v1 > 7.0f) v1 = 7.0f;
+                if (v1 < -8.0f) v1 = -8.0f;
+                unsigned lo = (unsigned)((int)v0 & 0xF), hi = (unsigned)((int)v1 & 0xF);
+                q[r * (cols / 2) + (g * gs + j) / 2] = (uint8_t)(lo | (hi << 4));
+            }
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* integer group dots                                                        */
+
+/* weight element k of a row, as a signed integer */
+static inline int wval(const uint8_t* row, int64_t k, int kind) {
+    if (kind == 8) return (int)row[k] - 128;                 /* quantize_int8.py:62 bias */
+    unsigned byte = row[k >> 1];                             /* quantize_int4.py:47-50  */
+    unsigned nib = (k & 1) ? (byte >> 4) : (byte & 0xF);
+    return ((int)(nib ^ 8u)) - 8;                            /* v5 run.cu:253 sign extend */
+}
+
+static inline size_t row_bytes(int64_t cols, int kind) {
+    return kind == 8 ? (size_t)cols : (size_t)cols / 2;
+}
+
+void orc_group_dots(int32_t* D, const uint8_t* wq, const int8_t* xq,
+                    int64_t rows, int64_t cols, int gs, int kind) {
+    int64_t ng = cols / gs;
+    size_t rb = row_bytes(cols, kind);
+    for (int64_t r = 0; r < rows; r++) {
+        const uint8_t* row = wq + (size_t)r * rb;
+        for (int64_t g = 0; g < ng; g++) {
+            int32_t d = 0;
+            for (int j = 0; j < gs; j++) {
+                int64_t k = g * gs + j;
+                d += wval(row, k, kind) * (int32_t)xq[k];
+            }
+            D[r * ng + g] = d;
+        }
+    }
+}
+
+void orc_gemv(float* out, const int8_t* xq, const float* xs, const uint8_t* wq,
+              const float* ws, int64_t rows, int64_t cols, int gs, int kind) {
+    int64_t ng = cols / gs;
+    size_t rb = row_bytes(cols, kind);
+    for (int64_t r = 0; r < rows; r++) {
+        const uint8_t* row = wq + (size_t)r * rb;
+        float acc = 0.0f;
+        for (int64_t g = 0; g < ng; g++) {
+            int32_t d = 0;
+            for (int j = 0; j < gs; j++) {
+                int64_t k = g * gs + j;
+                d += wval(row, k, kind) * (int32_t)xq[k];
+            }
+            acc += (ws[r * ng + g] * xs[g]) * (float)d;
+        }
+        out[r] = acc;
+    }
+}
+
+void orc_gemm(float* out, const int8_t* xq, const float* xs, const uint8_t* wq,
+              const float* ws, int B, int64_t rows, int64_t cols, int gs, int kind) {
+    int64_t ng = cols / gs;
+    for (int b = 0; b < B; b++)
+        orc_gemv(out + (size_t)b * rows, xq + (size_t)b * cols, xs + (size_t)b * ng,
+                 wq, ws, rows, cols, gs, kind);
+}
+
+/* ------------------------------------------------------------------------ */
+/* model: checkpoint reader (runq.c:230-278, v5 run.cu:534-551, plus the     */
+/* GS-carrying version-3 header of the product library) and forward        */
+
+typedef struct {
+    uint8_t* q;
+    float* s;
+    int64_t rows, cols;
+} OrcQ;
+
+struct OrcModel {
+    OrcConfig c;
+    int kind, gs;
+    float *emb, *rms_att, *rms_ffn, *rms_final;
+    OrcQ wq, wk, wv, wo, w1, w2, w3, wcls;
+    uint8_t* file;      /* whole file in memory */
+    uint8_t* own_wcls_q;
+    float* own_wcls_s;
+    /* run state */
+    int max_seq;
+    float *x, *xb, *xb2, *hb, *hb2, *q, *att, *logits, *kc, *vc;
+    int8_t* aq;
+    float* as;
+};
+
+static int take(uint8_t** p, uint8_t* end, size_t n, void** out) {
+    if ((size_t)(end - *p) < n) return -1;
+    *out = *p;
+    *p += n;
+    return 0;
+}
+
+static int take_q(uint8_t** p, uint8_t* end, OrcQ* w, int64_t rows, int64_t cols, int gs, int kind) {
+    w->rows = rows;
+    w->cols = cols;
+    if (take(p, end, (size_t)rows * row_bytes(cols, kind), (void**)&w->q)) return -1;
+    if (take(p, end, (size_t)rows * (cols / gs) * sizeof(float), (void**)&w->s)) return -1;
+    return 0;
+}
+
+OrcModel* orc_model_load(const char* path, int max_seq) {
+    FILE* f = fopen(path, "rb");
+    if (!f) { fprintf(stderr, "oracle: cannot open %s\n", path); return NULL; }
+    fseek(f, 0, SEEK_END);
+    long size = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    OrcModel* m = (OrcModel*)calloc(1, sizeof(OrcModel));
+    m->file = (uint8_t*)malloc((size_t)size);
+    if (fread(m->file, 1, (size_t)size, f) != (size_t)size) {
+        fclose(f);
+        orc_model_free(m);
+        return NULL;
+    }
+    fclose(f);
+    uint8_t* p = m->file;
+    uint8_t* end = m->file + size;
+    uint32_t magic, version;
+    memcpy(&magic, p, 4);
+    memcpy(&version, p + 4, 4);
+    p += 8;
+    if (magic == 0x384C4C51u && (version == 1 || version == 3)) m->kind = 8;
+    else if (magic == 0x344C4C51u && (version == 2 || version == 3)) m->kind = 4;
+    else { fprintf(stderr, "oracle: bad magic/version\n"); orc_model_free(m); return NULL; }
+    int32_t cfg[7];
+    memcpy(cfg, p, 28);
+    p += 28;
+    m->gs = 32;
+    if (version == 3) { int32_t g; memcpy(&g, p, 4); p += 4; m->gs = g; }
+    int shared = cfg[5] > 0;
+    m->c.dim = cfg[0]; m->c.hidden_dim = cfg[1]; m->c.n_layers = cfg[2];
+    m->c.n_heads = cfg[3]; m->c.n_kv_heads = cfg[4];
+    m->c.vocab_size = abs(cfg[5]); m->c.seq_len = cfg[6];
+    OrcConfig* c = &m->c;
+    int kv_dim = c->dim * c->n_kv_heads / c->n_heads;
+    int64_t L = c->n_layers;
+    int gs = m->gs, k = m->kind;
+    int bad = 0;
+    bad |= take(&p, end, (size_t)c->vocab_size * c->dim * 4, (void**)&m->emb);
+    bad |= take(&p, end, (size_t)L * c->dim * 4, (void**)&m->rms_att);
+    bad |= take_q(&p, end, &m->wq, L * c->dim, c->dim, gs, k);
+    bad |= take_q(&p, end, &m->wk, L * kv_dim, c->dim, gs, k);
+    bad |= take_q(&p, end, &m->wv, L * kv_dim, c->dim, gs, k);
+    bad |= take_q(&p, end, &m->wo, L * c->dim, c->dim, gs, k);
+    bad |= take(&p, end, (size_t)L * c->dim * 4, (void**)&m->rms_ffn);
+    bad |= take_q(&p, end, &m->w1, L * c->hidden_dim, c->dim, gs, k);
+    bad |= take_q(&p, end, &m->w2, L * c->dim, c->hidden_dim, gs, k);
+    bad |= take_q(&p, end, &m->w3, L * c->hidden_dim, c->dim, gs, k);
+    bad |= take(&p, end, (size_t)c->dim * 4, (void**)&m->rms_final);
+    if (!shared) {
+        bad |= take_q(&p, end, &m->wcls, c->vocab_size, c->dim, gs, k);
+    } else {
+        /* shared classifier: quantize the fp32 embedding with the same
+         * weight quantizer (extension; the reference exits here, runq.c:247) */
+        int64_t V = c->vocab_size, D = c->dim;
+        m->own_wcls_q = (uint8_t*)malloc((size_t)V * row_bytes(D, k));
+        m->own_wcls_s = (float*)malloc((size_t)V * (D / gs) * 4);
+        if (k == 8) orc_quantize_w8(m->emb, V, D, gs, m->own_wcls_q, m->own_wcls_s);
+        else orc_quantize_w4(m->emb, V, D, gs, m->own_wcls_q, m->own_wcls_s);
+        m->wcls.q = m->own_wcls_q; m->wcls.s = m->own_wcls_s;
+        m->wcls.rows = V; m->wcls.cols = D;
+    }
+    if (bad) { fprintf(stderr, "oracle: truncated checkpoint\n"); orc_model_free(m); return NULL; }
+    m->max_seq = (max_seq > 0 && max_seq < c->seq_len) ? max_seq : c->seq_len;
+    int maxn = c->hidden_dim > c->dim ? c->hidden_dim : c->dim;
+    m->x = (float*)calloc(c->dim, 4);
+    m->xb = (float*)calloc(c->dim, 4);
+    m->xb2 = (float*)calloc(c->dim, 4);
+    m->hb = (float*)calloc(c->hidden_dim, 4);
+    m->hb2 = (float*)calloc(c->hidden_dim, 4);
+    m->q = (float*)calloc(c->dim, 4);
+    m->att = (float*)calloc((size_t)c->n_heads * m->max_seq, 4);
+    m->logits = (float*)calloc(c->vocab_size, 4);
+    m->kc = (float*)calloc((size_t)L * m->max_seq * kv_dim, 4);
+    m->vc = (float*)calloc((size_t)L * m->max_seq * kv_dim, 4);
+    m->aq = (int8_t*)calloc(maxn, 1);
+    m->as = (float*)calloc(maxn / gs + 1, 4);
+    return m;
+}
+
+void orc_model_free(OrcModel* m) {
+    if (!m) return;
+    free(m->file); free(m->own_wcls_q); free(m->own_wcls_s);
+    free(m->x); free(m->xb); free(m->xb2); free(m->hb); free(m->hb2); free(m->q);
+    free(m->att); free(m->logits); free(m->kc); free(m->vc); free(m->aq); free(m->as);
+    free(m);
+}
+
+void orc_model_info(const OrcModel* m, OrcConfig* cfg, int* kind, int* gs) {
+    if (cfg) *cfg = m->c;
+    if (kind) *kind = m->kind;
+    if (gs) *gs = m->gs;
+}
+
+/* rmsnorm, runq.c:294-305.  The reference sums squares in 16 fp32 lanes with
+ * fused multiply-add and reduces them with _mm512_reduce_add_ps; the same
+ * lane order is kept here (tree: lanes i and i+8, then i and i+4, then pairs)
+ * so that the oracle tracks runq.c closely. */
+static void rmsnorm(float* o, const float* x, const float* w, int n) {
+    float lane[16] = {0};
+    int j = 0;
+    for (; j + 16 <= n; j += 16)
+        for (int i = 0; i < 16; i++) lane[i] = fmaf(x[j + i], x[j + i], lane[i]);
+    float t8[8], t4[4];
+    for (int i = 0; i < 8; i++) t8[i] = lane[i] + lane[i + 8];
+    for (int i = 0; i < 4; i++) t4[i] = t8[i] + t8[i + 4];
+    float s = (t4[0] + t4[2]) + (t4[1] + t4[3]);
+    for (; j < n; j++) s += x[j] * x[j];
+    s = 1.0f / sqrtf(s / n + 1e-5f);
+    for (int i = 0; i < n; i++) o[i] = w[i] * (s * x[i]);
+}
+
+static void softmax(float* x, int n) {   /* runq.c:307-318 */
+    float mx = x[0];
+    for (int i = 1; i < n; i++) if (x[i] > mx) mx = x[i];
+    float sum = 0.0f;
+    for (int i = 0; i < n; i++) { x[i] = expf(x[i] - mx); sum += x[i]; }
+    for (int i = 0; i < n; i++) x[i] /= sum;
+}
+
+static void qmatmul(OrcModel* m, float* out, const OrcQ* w, int64_t l, int64_t layer_rows, int n) {
+    size_t rb = row_bytes(w->cols, m->kind);
+    const uint8_t* q = w->q + (size_t)l * layer_rows * rb;
+    const float* s = w->s + (size_t)l * layer_rows * (w->cols / m->gs);
+    orc_gemv(out, m->aq, m->as, q, s, layer_rows, n, m->gs, m->kind);
+}
+
+float* orc_forward(OrcModel* m, int token, int pos) {
+    OrcConfig* p = &m->c;
+    int dim = p->dim, hidden = p->hidden_dim, hs = dim / p->n_heads;
+    int kv_dim = dim * p->n_kv_heads / p->n_heads, kv_mul = p->n_heads / p->n_kv_heads;
+    int gs = m->gs;
+    float* x = m->x;
+    memcpy(x, m->emb + (size_t)token * dim, dim * 4);            /* runq.c:332-333 */
+    for (int64_t l = 0; l < p->n_layers; l++) {
+        rmsnorm(m->xb, x, m->rms_att + l * dim, dim);             /* :338 */
+        size_t loff = (size_t)l * m->max_seq * kv_dim;
+        float* k = m->kc + loff + (size_t)pos * kv_dim;
+        float* v = m->vc + loff + (size_t)pos * kv_dim;
+        orc_quantize_act(m->xb, dim, gs, m->aq, m->as, NULL);     /* :345 */
+        qmatmul(m, m->q, &m->wq, l, dim, dim);                     /* :346-348 */
+        qmatmul(m, k, &m->wk, l, kv_dim, dim);
+        qmatmul(m, v, &m->wv, l, kv_dim, dim);
+        for (int i = 0; i < dim; i += 2) {                         /* RoPE :351-365 */
+            int hd = i % hs;
+            float freq = 1.0f / powf(10000.0f, hd / (float)hs);
+            float val = pos * freq;
+            float fcr = cosf(val), fci = sinf(val);
+            int rotn = i < kv_dim ? 2 : 1;
+            for (int r = 0; r < rotn; r++) {
+                float* vec = r == 0 ? m->q : k;
+                float v0 = vec[i], v1 = vec[i + 1];
+                vec[i] = v0 * fcr - v1 * fci;
+                vec[i + 1] = v0 * fci + v1 * fcr;
+            }
+        }
+        for (int h = 0; h < p->n_heads; h++) {                     /* attention :369-391 */
+            float* qh = m->q + h * hs;
+            float* att = m->att + (size_t)h * m->max_seq;
+            for (int t = 0; t <= pos; t++) {
+                float* kt = m->kc + loff + (size_t)t * kv_dim + (h / kv_mul) * hs;
+                float sc = 0.0f;
+                for (int i = 0; i < hs; i++) sc += qh[i] * kt[i];
+                att[t] = sc / sqrtf(hs);
+            }
+            softmax(att, pos + 1);
+            float* xb = m->xb + h * hs;
+            memset(xb, 0, hs * 4);
+            for (int t = 0; t <= pos; t++) {
+                float* vt = m->vc + loff + (size_t)t * kv_dim + (h / kv_mul) * hs;
+                float a = att[t];
+                for (int i = 0; i < hs; i++) xb[i] += a * vt[i];
+            }
+        }
+        orc_quantize_act(m->xb, dim, gs, m->aq, m->as, NULL);     /* :394-396 */
+        qmatmul(m, m->xb2, &m->wo, l, dim, dim);
+        for (int i = 0; i < dim; i++) x[i] += m->xb2[i];
+        rmsnorm(m->xb, x, m->rms_ffn + l * dim, dim);              /* :399-402 */
+        orc_quantize_act(m->xb, dim, gs, m->aq, m->as, NULL);
+        qmatmul(m, m->hb, &m->w1, l, hidden, dim);
+        qmatmul(m, m->hb2, &m->w3, l, hidden, dim);
+        for (int i = 0; i < hidden; i++) {                         /* SwiGLU :405-410 */
+            float val = m->hb[i];
+            val *= (1.0f / (1.0f + expf(-val)));
+            val *= m->hb2[i];
+            m->hb[i] = val;
+        }
+        orc_quantize_act(m->hb, hidden, gs, m->aq, m->as, NULL);  /* :412-414 */
+        qmatmul(m, m->xb, &m->w2, l, dim, hidden);
+        for (int i = 0; i < dim; i++) x[i] += m->xb[i];
+    }
+    rmsnorm(x, x, m->rms_final, dim);                              /* :417-419 */
+    orc_quantize_act(x, dim, gs, m->aq, m->as, NULL);
+    orc_gemv(m->logits, m->aq, m->as, m->wcls.q, m->wcls.s, p->vocab_size, dim, gs, m->kind);
+    return m->logits;
+}
+
+int orc_argmax(const float* v, int n) {                            /* runq.c:578-585 */
+    int mi = 0;
+    float mv = v[0];
+    for (int i = 1; i < n; i++) if (v[i] > mv) { mi = i; mv = v[i]; }
+    return mi;
+}
