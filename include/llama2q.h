@@ -86,6 +86,13 @@ int lq_sync(void);
 #define LQ_LAUNCH_PDL 1
 int lq_set_launch_flags(int flags);
 
+/* Tracing: when set, every GEMV launched by quantize/matmul/matmul_f32
+ * writes four globaltimer stamps (ns) per CTA into device_buffer
+ * ([grid][4]: start, dependency satisfied, activation staged, end); NULL
+ * turns it off.  The buffer must hold 4 x 148 x 8 bytes per launch and is
+ * overwritten by each launch. */
+int lq_set_trace(void* device_buffer);
+
 /* Stream capture of operator calls into a CUDA graph on the library stream
  * (the reference captures its forward the same way,
  * v5-cuda-fused/run.cu:671-679).  lq_graph_end returns an executable graph

@@ -79,7 +79,7 @@ class Config(C.Structure):
 # names the C ABI exports (checked by the CPU test suite against the header)
 EXPORTS = (
     "lq_last_error", "lq_select_device", "lq_set_stream", "lq_get_stream", "lq_sync",
-    "lq_set_launch_flags", "lq_graph_begin", "lq_graph_end", "lq_graph_launch", "lq_graph_destroy",
+    "lq_set_launch_flags", "lq_set_trace", "lq_graph_begin", "lq_graph_end", "lq_graph_launch", "lq_graph_destroy",
     "lq_synth_tensor", "quantize", "matmul", "matmul_f32",
     "build_transformer", "build_transformer_random", "forward", "forward_argmax",
     "free_transformer", "transformer_config",
@@ -107,6 +107,7 @@ def lib() -> C.CDLL:
         "lq_get_stream": (P, []),
         "lq_sync": (I, []),
         "lq_set_launch_flags": (I, [I]),
+        "lq_set_trace": (I, [P]),
         "lq_graph_begin": (I, []),
         "lq_graph_end": (I, [C.POINTER(P)]),
         "lq_graph_launch": (I, [P]),
@@ -158,6 +159,10 @@ LAUNCH_PDL = 1
 
 def set_launch_flags(flags: int) -> None:
     check(lib().lq_set_launch_flags(flags))
+
+
+def set_trace(device_ptr: int | None) -> None:
+    check(lib().lq_set_trace(device_ptr))
 
 
 def graph_begin() -> None:

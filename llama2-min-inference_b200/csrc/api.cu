@@ -15,6 +15,7 @@ namespace {
 thread_local char g_err[1024] = "";
 cudaStream_t g_stream = nullptr;
 int g_launch_flags = 0;
+uint64_t* g_trace = nullptr;  // device buffer for per-CTA GEMV phase timestamps (lq_set_trace)
 std::mutex g_ctx_mu;
 lq::DevCtx* g_ctx[64] = {nullptr};
 
@@ -63,6 +64,11 @@ DevCtx* ctx() {
 
 int ensure_scratch(DevCtx* c, size_t bytes) {
     if (c->scratch_bytes >= bytes) return LQ_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(g_stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+        return lq_fail(LQ_EINVAL,
+                       "scratch of %zu bytes needed inside a graph capture: make one call of this size before capturing",
+                       bytes);
     if (c->scratch) cudaFree(c->scratch);
     c->scratch = nullptr;
     c->scratch_bytes = 0;
@@ -86,6 +92,40 @@ int check_device_error(int* err_dev, cudaStream_t st) {
 }
 
 cudaStream_t stream() { return g_stream; }
+
+// quantize x into (xq, xs, xsum), then the GEMV from the pre-quantized
+// activation; the GEMV may start streaming weights while the quantizer runs
+int matmul_f32_device(float* yd, const float* xd, const QuantizedTensor* w, int n, int d, int8_t* xq, float* xs,
+                      int* xsum, int* err, cudaStream_t st, bool pdl_first, int num_sms, uint64_t* trace) {
+    ActQuantArgs q = {};
+    q.mode = IN_F32;
+    q.n = n;
+    q.gs = w->group_size;
+    q.nb = 1;
+    q.x = xd;
+    q.xq = xq;
+    q.xs = xs;
+    q.xsum = xsum;
+    cudaError_t e = act_quant_launch(q, st, pdl_first);
+    if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: quantize launch");
+    GemvArgs a = {};
+    a.seg[0] = {static_cast<const uint8_t*>(w->q), w->s, yd, d, EPI_STORE};
+    a.nseg = 1;
+    a.cols = n;
+    a.gs = w->group_size;
+    a.nb = 1;
+    a.in_mode = IN_QUANT;
+    a.xq = xq;
+    a.xs = xs;
+    a.xsum_in = xsum;
+    a.y_stride = d;
+    a.err = err;
+    a.trace = trace;
+    // the quantizer does not write the weights, so the GEMV may prefetch them
+    e = gemv_launch(a, w->kind, st, true, num_sms);
+    if (e != cudaSuccess) return cuda_fail(e, "matmul_f32 launch");
+    return LQ_OK;
+}
 
 }  // namespace lq
 
@@ -139,6 +179,11 @@ int lq_sync(void) {
 int lq_set_launch_flags(int flags) {
     if (flags & ~LQ_LAUNCH_PDL) return lq_fail(LQ_EINVAL, "unknown launch flags 0x%x", flags);
     g_launch_flags = flags;
+    return LQ_OK;
+}
+
+int lq_set_trace(void* device_buffer) {
+    g_trace = static_cast<uint64_t*>(device_buffer);
     return LQ_OK;
 }
 
@@ -252,6 +297,7 @@ int matmul(float* xout, const QuantizedTensor* x, const QuantizedTensor* w, int 
         a.xs = x->s + done * ng;
         a.y_stride = d;
         a.err = c->err;
+        a.trace = g_trace;
         cudaError_t e = gemv_launch(a, w->kind, g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms);
         if (e != cudaSuccess) return cuda_fail(e, "matmul launch");
         done += nb;
@@ -266,37 +312,30 @@ int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int
     DevCtx* c = ctx();
     if (!c) return lq_fail(LQ_ECUDA, "no CUDA device context (no device, or first use inside a graph capture)");
     const bool xdev = is_device_ptr(x), ydev = is_device_ptr(xout);
+    const int ng = n / w->group_size;
+    // scratch: [fp32 x (host input only)] [int8 xq] [fp32 xs] [int32 xsum] [fp32 y (host output only)]
+    const size_t off_xq = xdev ? 0 : ((size_t)n * 4 + 255) / 256 * 256;
+    const size_t off_xs = off_xq + ((size_t)n + 255) / 256 * 256;
+    const size_t off_xsum = off_xs + ((size_t)ng * 4 + 255) / 256 * 256;
+    const size_t off_y = off_xsum + ((size_t)ng * 4 + 255) / 256 * 256;
+    rc = ensure_scratch(c, off_y + (ydev ? 0 : (size_t)d * 4));
+    if (rc) return rc;
+    char* sc = static_cast<char*>(c->scratch);
     const float* xd = x;
-    float* yd = xout;
-    if (!xdev || !ydev) {
-        const size_t xb = ((size_t)n * 4 + 255) / 256 * 256;
-        rc = ensure_scratch(c, xb + (size_t)d * 4);
-        if (rc) return rc;
-        if (!xdev) {
-            cudaError_t e = cudaMemcpyAsync(c->scratch, x, (size_t)n * 4, cudaMemcpyHostToDevice, g_stream);
-            if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of x");
-            xd = static_cast<const float*>(c->scratch);
-        }
-        if (!ydev) yd = reinterpret_cast<float*>(static_cast<char*>(c->scratch) + xb);
+    float* yd = ydev ? xout : reinterpret_cast<float*>(sc + off_y);
+    if (!xdev) {
+        cudaError_t e = cudaMemcpyAsync(sc, x, (size_t)n * 4, cudaMemcpyHostToDevice, g_stream);
+        if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of x");
+        xd = reinterpret_cast<const float*>(sc);
     }
-    GemvArgs a = {};
-    a.seg[0] = {static_cast<const uint8_t*>(w->q), w->s, yd, d, EPI_STORE};
-    a.nseg = 1;
-    a.cols = n;
-    a.gs = w->group_size;
-    a.nb = 1;
-    a.in_mode = IN_F32;
-    a.xf = xd;
-    a.y_stride = d;
-    a.err = c->err;
-    cudaError_t e = gemv_launch(a, w->kind, g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms);
-    if (e != cudaSuccess) return cuda_fail(e, "matmul_f32 launch");
+    rc = lq::matmul_f32_device(yd, xd, w, n, d, reinterpret_cast<int8_t*>(sc + off_xq),
+                               reinterpret_cast<float*>(sc + off_xs), reinterpret_cast<int*>(sc + off_xsum),
+                               c->err, g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms, g_trace);
+    if (rc) return rc;
     if (!xdev || !ydev) {
-        if (!ydev) {
-            e = cudaMemcpyAsync(xout, yd, (size_t)d * 4, cudaMemcpyDeviceToHost, g_stream);
-            if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of xout");
-        }
-        e = cudaStreamSynchronize(g_stream);
+        cudaError_t e = cudaSuccess;
+        if (!ydev) e = cudaMemcpyAsync(xout, yd, (size_t)d * 4, cudaMemcpyDeviceToHost, g_stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(g_stream);
         if (e != cudaSuccess) return cuda_fail(e, "matmul_f32");
     }
     return LQ_OK;

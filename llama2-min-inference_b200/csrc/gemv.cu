@@ -58,7 +58,7 @@ __host__ __device__ inline Layout make_layout(const GemvArgs& a) {
     const int ng = a.cols / a.gs;
     L.off_bars = 0;
     L.off_red = align_up(a.nstages * 8, 16);
-    L.off_x = align_up(L.off_red + kW * 4, 128);
+    L.off_x = align_up(L.off_red + 32 * 4, 128);
     L.off_xs = align_up(L.off_x + a.x_bytes, 16);
     L.off_xsum = align_up(L.off_xs + a.nb * ng * 4, 16);
     L.off_stage = align_up(L.off_xsum + a.nb * ng * 4, 128);
@@ -66,6 +66,8 @@ __host__ __device__ inline Layout make_layout(const GemvArgs& a) {
     L.total = L.off_stage + a.nstages * L.stage_bytes;
     return L;
 }
+
+__host__ __device__ inline bool gs_ok_dev(int gs) { return gs == 32 || gs == 64 || gs == 128 || gs == 256; }
 
 // ---------------------------------------------------------------------------
 // activation prologue
@@ -89,128 +91,164 @@ __device__ __forceinline__ int quant_div(float x, float s, float rcp) {
 }
 
 // Deterministic sum over the consumer threads (same order in every CTA).
-__device__ float consumer_sum(float v, float* red, int ctid) {
+__device__ float consumer_sum(float v, float* red, int ctid, int nt) {
     v = warp_sum(v);
     if ((ctid & 31) == 0) red[ctid >> 5] = v;
-    named_bar_sync(1, kCT);
+    named_bar_sync(1, nt);
     float s = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kW; ++w) s += red[w];
-    named_bar_sync(1, kCT);
+    for (int w = 0; w < nt / 32; ++w) s += red[w];
+    named_bar_sync(1, nt);
     return s;
 }
 
 template <int KIND>
-__device__ void stage_input(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum, float* red, int ctid) {
+__device__ void stage_input(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum, float* red, int ctid, int nt) {
     const int n = a.cols, gs = a.gs, ng = n / gs;
     if (a.in_mode == IN_QUANT) {
-        // copy int8 rows (INT4: split into even/odd planes), 8 bytes a step
+        // copy int8 rows (INT4: split into even/odd planes), 8 bytes a step;
+        // every load of this thread is issued before any store
         const int total8 = a.nb * n / 8;
-        for (int i = ctid; i < total8; i += kCT) {
-            const uint2 v = reinterpret_cast<const uint2*>(a.xq)[i];
-            const int b = (i * 8) / n, k0 = i * 8 - b * n;
-            int8_t* xrow = xsm + (size_t)b * n;
-            if (KIND == 4) {
-                *reinterpret_cast<uint32_t*>(xrow + (k0 >> 1)) = __byte_perm(v.x, v.y, 0x6420);
-                *reinterpret_cast<uint32_t*>(xrow + (n >> 1) + (k0 >> 1)) = __byte_perm(v.x, v.y, 0x7531);
-            } else {
-                *reinterpret_cast<uint2*>(xrow + k0) = v;
+        constexpr int U = 4;
+        for (int i0 = ctid; i0 < total8; i0 += U * nt) {
+            uint2 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * nt;
+                if (i < total8) v[u] = reinterpret_cast<const uint2*>(a.xq)[i];
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int i = i0 + u * nt;
+                if (i >= total8) break;
+                const int b = (i * 8) / n, k0 = i * 8 - b * n;
+                int8_t* xrow = xsm + (size_t)b * n;
+                if (KIND == 4) {
+                    *reinterpret_cast<uint32_t*>(xrow + (k0 >> 1)) = __byte_perm(v[u].x, v[u].y, 0x6420);
+                    *reinterpret_cast<uint32_t*>(xrow + (n >> 1) + (k0 >> 1)) = __byte_perm(v[u].x, v[u].y, 0x7531);
+                } else {
+                    *reinterpret_cast<uint2*>(xrow + k0) = v[u];
+                }
             }
         }
-        for (int g = ctid; g < a.nb * ng; g += kCT) {
-            const int4* q = reinterpret_cast<const int4*>(a.xq + (size_t)g * gs);
-            int s = 0;
-            for (int j = 0; j < gs / 16; ++j) {
-                const int4 v = q[j];
-                s = __dp4a(v.x, 0x01010101, s);
-                s = __dp4a(v.y, 0x01010101, s);
-                s = __dp4a(v.z, 0x01010101, s);
-                s = __dp4a(v.w, 0x01010101, s);
+        if (a.xsum_in) {
+            for (int g = ctid; g < a.nb * ng; g += nt) {
+                xs[g] = a.xs[g];
+                xsum[g] = a.xsum_in[g];
             }
-            xs[g] = a.xs[g];
-            xsum[g] = s;
+        } else {
+            named_bar_sync(1, nt);
+            // group sums from the staged copy (INT4: the group's even and odd
+            // values are two contiguous runs of gs/2 bytes, one per plane)
+            for (int g = ctid; g < a.nb * ng; g += nt) {
+                const int b = g / ng, gg = g - b * ng;
+                const int8_t* xrow = xsm + (size_t)b * n;
+                int s = 0;
+                if (KIND == 4) {
+                    const int* p0 = reinterpret_cast<const int*>(xrow + gg * (gs / 2));
+                    const int* p1 = reinterpret_cast<const int*>(xrow + (n >> 1) + gg * (gs / 2));
+                    for (int j = 0; j < gs / 8; ++j) s = __dp4a(p1[j], 0x01010101, __dp4a(p0[j], 0x01010101, s));
+                } else {
+                    const int* p0 = reinterpret_cast<const int*>(xrow + gg * gs);
+                    for (int j = 0; j < gs / 4; ++j) s = __dp4a(p0[j], 0x01010101, s);
+                }
+                xs[g] = a.xs[g];
+                xsum[g] = s;
+            }
         }
         return;
     }
+    constexpr int MAXR = 8;  // rounds of 8 values per thread held in registers
+    const bool norm = a.in_mode == IN_RMSNORM || a.in_mode == IN_RMSNORM_EMB;
+    const int lpg = gs / 8;   // lanes per group: 4, 8, 16 or 32
+    const int tasks = ng * lpg;
     for (int b = 0; b < a.nb; ++b) {
         const float* src = a.xf ? a.xf + (size_t)b * n : nullptr;
-        float inv = 1.0f;
         if (a.in_mode == IN_RMSNORM_EMB) {
             const int token = a.meta[2 * b];
             src = a.emb + (size_t)token * n;
             if (blockIdx.x == 0)
-                for (int i = ctid; i < n; i += kCT) a.x_out[(size_t)b * n + i] = src[i];
-        }
-        const bool norm = a.in_mode == IN_RMSNORM || a.in_mode == IN_RMSNORM_EMB;
-        if (norm) {
-            // rmsnorm, v1-int8-vnni/runq.c:294-305: 1/sqrt(mean(x^2) + 1e-5);
-            // thread t sums float4 chunks t, t+256, ... in order
-            float ss = 0.0f;
-            for (int c = ctid; c < n / 4; c += kCT) {
-                const float4 v = reinterpret_cast<const float4*>(src)[c];
-                ss = fmaf(v.x, v.x, ss);
-                ss = fmaf(v.y, v.y, ss);
-                ss = fmaf(v.z, v.z, ss);
-                ss = fmaf(v.w, v.w, ss);
-            }
-            ss = consumer_sum(ss, red, ctid);
-            inv = 1.0f / sqrtf(ss / (float)n + 1e-5f);
+                for (int i = ctid; i < n; i += nt) a.x_out[(size_t)b * n + i] = src[i];
         }
         int8_t* xrow = xsm + (size_t)b * n;
-        // quantize_act, runq.c:117-139: eight lanes per group, eight values
-        // per lane (group max and sum over the eight lanes by xor shuffles)
-        const int lpg = gs / 8;  // lanes per group: 4, 8, 16 or 32
-        const int tasks = ng * lpg;
-        for (int t0 = 0; t0 < tasks; t0 += kCT) {
-            const int t = t0 + ctid;
-            const bool on = t < tasks;
-            const int k0 = (on ? t : 0) * 8;  // first of this lane's 8 values
-            float v[8];
-            float amax = 0.0f;
-            if (on) {
-                const float4 a0 = *reinterpret_cast<const float4*>(src + k0);
-                const float4 a1 = *reinterpret_cast<const float4*>(src + k0 + 4);
-                v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
-                v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
-                if (norm) {
-                    const float4 w0 = *reinterpret_cast<const float4*>(a.rms_w + k0);
-                    const float4 w1 = *reinterpret_cast<const float4*>(a.rms_w + k0 + 4);
-                    const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        for (int base = 0; base < tasks; base += MAXR * nt) {
+            // all of this thread's loads first (8 values per round), then the math
+            float v[MAXR][8];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) v[i] = w[i] * (inv * v[i]);
-                }
-#pragma unroll
-                for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
-            }
-            for (int o = 1; o < lpg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            float sc = amax / 127.0f;
-            if (sc == 0.0f) sc = 1e-8f;
-            const float rcp = 1.0f / sc;
-            int qs = 0;
-            uint32_t lo = 0, hi = 0;
-            if (on) {
-                int q[8];
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    q[i] = max(-127, min(127, quant_div(v[i], sc, rcp)));
-                    qs += q[i];
-                }
-                if (KIND == 4) {  // even values to plane 0, odd values to plane 1
-                    lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) | ((uint32_t)(q[6] & 0xFF) << 24);
-                    hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
-                    *reinterpret_cast<uint32_t*>(xrow + (k0 >> 1)) = lo;
-                    *reinterpret_cast<uint32_t*>(xrow + (n >> 1) + (k0 >> 1)) = hi;
+            for (int r = 0; r < MAXR; ++r) {
+                const int t = base + r * nt + ctid;
+                if (t < tasks) {
+                    const float4 a0 = *reinterpret_cast<const float4*>(src + t * 8);
+                    const float4 a1 = *reinterpret_cast<const float4*>(src + t * 8 + 4);
+                    v[r][0] = a0.x; v[r][1] = a0.y; v[r][2] = a0.z; v[r][3] = a0.w;
+                    v[r][4] = a1.x; v[r][5] = a1.y; v[r][6] = a1.z; v[r][7] = a1.w;
                 } else {
-                    lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
-                    hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
-                    *reinterpret_cast<uint2*>(xrow + k0) = make_uint2(lo, hi);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) v[r][i] = 0.0f;
                 }
             }
-            for (int o = 1; o < lpg; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
-            if (on && (t & (lpg - 1)) == 0) {
-                const int g = t / lpg;
-                xs[b * ng + g] = sc;
-                xsum[b * ng + g] = qs;
+            if (norm) {
+                // rmsnorm, v1-int8-vnni/runq.c:294-305: 1/sqrt(mean(x^2) + 1e-5).
+                // Requires the whole vector in one pass (n <= MAXR*8*256).
+                float ss = 0.0f;
+#pragma unroll
+                for (int r = 0; r < MAXR; ++r)
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) ss = fmaf(v[r][i], v[r][i], ss);
+                ss = consumer_sum(ss, red, ctid, nt);
+                const float inv = 1.0f / sqrtf(ss / (float)n + 1e-5f);
+#pragma unroll
+                for (int r = 0; r < MAXR; ++r) {
+                    const int t = base + r * nt + ctid;
+                    if (t < tasks) {
+                        const float4 w0 = *reinterpret_cast<const float4*>(a.rms_w + t * 8);
+                        const float4 w1 = *reinterpret_cast<const float4*>(a.rms_w + t * 8 + 4);
+                        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) v[r][i] = w[i] * (inv * v[r][i]);
+                    }
+                }
+            }
+            // quantize_act, runq.c:117-139: a group spans lpg lanes (8 values
+            // each); group max and sum by xor shuffles over those lanes
+#pragma unroll
+            for (int r = 0; r < MAXR; ++r) {
+                const int t = base + r * nt + ctid;
+                if (base + r * nt >= tasks) break;  // uniform across the block
+                const bool on = t < tasks;
+                const int k0 = (on ? t : 0) * 8;
+                float amax = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[r][i]));
+                for (int o = 1; o < lpg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+                float sc = amax / 127.0f;
+                if (sc == 0.0f) sc = 1e-8f;
+                const float rcp = 1.0f / sc;
+                int qs = 0;
+                if (on) {
+                    int q[8];
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        q[i] = max(-127, min(127, quant_div(v[r][i], sc, rcp)));
+                        qs += q[i];
+                    }
+                    uint32_t lo, hi;
+                    if (KIND == 4) {  // even values to plane 0, odd values to plane 1
+                        lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) | ((uint32_t)(q[6] & 0xFF) << 24);
+                        hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+                        *reinterpret_cast<uint32_t*>(xrow + (k0 >> 1)) = lo;
+                        *reinterpret_cast<uint32_t*>(xrow + (n >> 1) + (k0 >> 1)) = hi;
+                    } else {
+                        lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+                        hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+                        *reinterpret_cast<uint2*>(xrow + k0) = make_uint2(lo, hi);
+                    }
+                }
+                for (int o = 1; o < lpg; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+                if (on && (t & (lpg - 1)) == 0) {
+                    const int g = t / lpg;
+                    xs[b * ng + g] = sc;
+                    xsum[b * ng + g] = qs;
+                }
             }
         }
     }
@@ -232,16 +270,21 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const int8_t* xrow, int 
     } else {
         const uint4 xe = *reinterpret_cast<const uint4*>(xrow + 16 * c);
         const uint4 xo = *reinterpret_cast<const uint4*>(xrow + (n >> 1) + 16 * c);
-        const uint32_t M = 0x0F0F0F0Fu, F = 0x08080808u;
-        d = dp4a_us((w.x ^ F) & M, xe.x, d);
-        d = dp4a_us(((w.x >> 4) ^ F) & M, xo.x, d);
-        d = dp4a_us((w.y ^ F) & M, xe.y, d);
-        d = dp4a_us(((w.y >> 4) ^ F) & M, xo.y, d);
-        d = dp4a_us((w.z ^ F) & M, xe.z, d);
-        d = dp4a_us(((w.z >> 4) ^ F) & M, xo.z, d);
-        d = dp4a_us((w.w ^ F) & M, xe.w, d);
-        d = dp4a_us(((w.w >> 4) ^ F) & M, xo.w, d);
-        return d;
+        // w ^ 0x88.. turns each two's-complement nibble into q+8; the low
+        // nibbles dot the even plane, the high nibbles (kept in place, i.e.
+        // 16*(q+8)) dot the odd plane into a second sum that is 16x
+        const uint32_t L4 = 0x0F0F0F0Fu, H4 = 0xF0F0F0F0u;
+        const uint32_t a0 = w.x ^ 0x88888888u, a1 = w.y ^ 0x88888888u, a2 = w.z ^ 0x88888888u,
+                       a3 = w.w ^ 0x88888888u;
+        int dl = dp4a_us(a0 & L4, xe.x, 0);
+        int dh = dp4a_us(a0 & H4, xo.x, 0);
+        dl = dp4a_us(a1 & L4, xe.y, dl);
+        dh = dp4a_us(a1 & H4, xo.y, dh);
+        dl = dp4a_us(a2 & L4, xe.z, dl);
+        dh = dp4a_us(a2 & H4, xo.z, dh);
+        dl = dp4a_us(a3 & L4, xe.w, dl);
+        dh = dp4a_us(a3 & H4, xo.w, dh);
+        return d + dl + (dh >> 4);
     }
 }
 
@@ -422,7 +465,7 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 4 : (NB == 2 ? 2 : 1))
         }
     }
     pdl_wait();
-    stage_input<KIND>(a, xsm, xs, xsum, red, threadIdx.x);
+    stage_input<KIND>(a, xsm, xs, xsum, red, threadIdx.x, blockDim.x);
     __syncthreads();
 
     constexpr int NR = CPG >= 4 ? 2 : 4;  // rows loaded together: 8 x 16 B per lane in flight (CPG <= 4)
@@ -508,14 +551,455 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 4 : (NB == 2 ? 2 : 1))
 }
 
 // ---------------------------------------------------------------------------
+// the bulk-copy (TMA) kernel, used when every scale row starts on a 16-byte
+// boundary (group count a multiple of 4, true for every Llama shape)
+//
+// One CTA per SM, eight warps.  Warp w of the grid owns the contiguous pair
+// range [w*P/W, (w+1)*P/W) and runs its own two-slot copy pipeline: lane 0
+// issues 1-D bulk copies (cp.async.bulk, the TMA engine) of the warp's next
+// item into a free slot, the warp computes the other slot from shared
+// memory.  An item is either K whole row pairs (short rows; one contiguous
+// copy per tensor) or one slice of both rows of a pair (long rows).  The
+// first two items are requested at kernel start — before the activation
+// prologue and, inside a model, before griddepcontrol.wait — so the weight
+// stream overlaps everything else.
+
+constexpr int kTmaMaxWarps = 16;
+constexpr int kSlotW = 8192;  // weight bytes per slot (all tensors)
+
+struct TItem {
+    int seg, row, nrows, boff, bytes;  // rows [row, row+nrows) of segment seg; slice [boff, boff+bytes)
+    bool last;                         // last slice of the pair (or whole rows)
+};
+
+// walks a warp's items in order; identical in every lane
+struct TIter {
+    int p, p1, j;  // pair index, end, slice index
+};
+
+__device__ __forceinline__ bool titem_next(const GemvArgs& a, TIter& it, int rb, TItem& o) {
+    if (it.p >= it.p1) return false;
+    int seg = 0, p = it.p, np = a.seg[0].rows >> 1;
+    while (p >= np) {
+        p -= np;
+        ++seg;
+        np = a.seg[seg].rows >> 1;
+    }
+    o.seg = seg;
+    o.row = 2 * p;
+    if (!a.split) {
+        const int k = min(min(a.stage_rows >> 1, np - p), it.p1 - it.p);
+        o.nrows = 2 * k;
+        o.boff = 0;
+        o.bytes = o.nrows * rb;
+        o.last = true;
+        it.p += k;
+    } else {
+        o.nrows = 2;
+        o.boff = it.j * a.slice_bytes;
+        o.bytes = min(a.slice_bytes, rb - o.boff);
+        o.last = o.boff + o.bytes == rb;
+        if (o.last) {
+            it.j = 0;
+            ++it.p;
+        } else {
+            ++it.j;
+        }
+    }
+    return true;
+}
+
+__device__ __forceinline__ void titem_issue(const GemvArgs& a, const TItem& it, uint8_t* slot, uint64_t* bar, int rb,
+                                            int ng, int gb, int tw, uint64_t pol) {
+    const GemvSeg& g = a.seg[it.seg];
+    const int mult = a.paired ? 2 : 1;
+    const int sb = (it.bytes / gb) * 4;  // scale bytes per row slice
+    uint8_t* sdst = slot + kSlotW;        // scales follow the weights
+    if (!a.split) {
+        const uint32_t wbytes = (uint32_t)(it.nrows * rb), sbytes = (uint32_t)(it.nrows * ng * 4);
+        mbar_arrive_expect_tx(bar, mult * (wbytes + sbytes));
+        bulk_g2s(slot, g.wq + (size_t)it.row * rb, wbytes, bar, pol);
+        bulk_g2s(sdst, g.ws + (size_t)it.row * ng, sbytes, bar, pol);
+        if (a.paired) {
+            bulk_g2s(slot + tw, g.wq2 + (size_t)it.row * rb, wbytes, bar, pol);
+            bulk_g2s(sdst + sbytes, g.ws2 + (size_t)it.row * ng, sbytes, bar, pol);
+        }
+    } else {
+        const int region = a.scap / (2 * mult);  // scale bytes reserved per (tensor, row)
+        mbar_arrive_expect_tx(bar, (uint32_t)(mult * 2 * (it.bytes + sb)));
+        for (int t = 0; t < mult; ++t) {
+            const uint8_t* wq = t ? g.wq2 : g.wq;
+            const float* ws = t ? g.ws2 : g.ws;
+            for (int h = 0; h < 2; ++h) {
+                const int r = it.row + h;
+                bulk_g2s(slot + t * tw + h * (tw / 2), wq + (size_t)r * rb + it.boff, (uint32_t)it.bytes, bar, pol);
+                bulk_g2s(sdst + (t * 2 + h) * region, ws + (size_t)r * ng + it.boff / gb, (uint32_t)sb, bar, pol);
+            }
+        }
+    }
+}
+
+// one warp, one row (slice) in shared memory: lane owns groups lane,
+// lane+32, ...; chunks read in a lane-rotated order (bank-conflict free)
+template <int KIND, int NB, int CPG>
+__device__ __forceinline__ void smem_row_dot(const uint8_t* w, const float* sc, int g0, int ngs, const int8_t* xsm,
+                                             const float* xs, const int* xsum, int n, int ng, int lane,
+                                             float acc[NB]) {
+    constexpr int BIAS = KIND == 8 ? 128 : 8;
+    const int rot = CPG >= 8 ? (lane & 7) : ((lane * CPG) >> 3) & (CPG - 1);
+    for (int gl = lane; gl < ngs; gl += 32) {
+        const uint8_t* wg = w + (size_t)gl * CPG * 16;
+        const int g = g0 + gl;
+        int d0[NB], d1[NB];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) d0[b] = d1[b] = 0;
+#pragma unroll
+        for (int k = 0; k < CPG; ++k) {
+            const int kk = (k + rot) & (CPG - 1);
+            const uint4 wv = *reinterpret_cast<const uint4*>(wg + 16 * kk);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                if (k & 1) d1[b] = chunk_dot<KIND>(wv, xsm + (size_t)b * n, g * CPG + kk, n, d1[b]);
+                else d0[b] = chunk_dot<KIND>(wv, xsm + (size_t)b * n, g * CPG + kk, n, d0[b]);
+            }
+        }
+        const float sw = sc[gl];
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const int D = d0[b] + d1[b] - BIAS * xsum[b * ng + g];
+            acc[b] = fmaf(sw * xs[b * ng + g], (float)D, acc[b]);
+        }
+    }
+}
+
+// R rows (slices of equal length) at once: the activation chunk is read
+// once for all R rows, and the R integer chains run side by side.
+template <int KIND, int NB, int CPG, int R>
+__device__ __forceinline__ void smem_rows_dot(const uint8_t* const* w, const float* const* sc, int g0, int ngs,
+                                              const int8_t* xsm, const float* xs, const int* xsum, int n, int ng,
+                                              int lane, float (*acc)[NB]) {
+    constexpr int BIAS = KIND == 8 ? 128 : 8;
+    const int rot = CPG >= 8 ? (lane & 7) : ((lane * CPG) >> 3) & (CPG - 1);
+    for (int gl = lane; gl < ngs; gl += 32) {
+        const int g = g0 + gl;
+        int d[R][NB];
+#pragma unroll
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+            for (int b = 0; b < NB; ++b) d[r][b] = 0;
+#pragma unroll
+        for (int k = 0; k < CPG; ++k) {
+            const int kk = (k + rot) & (CPG - 1);
+            const int c = g * CPG + kk;
+            uint4 wv[R];
+#pragma unroll
+            for (int r = 0; r < R; ++r) wv[r] = *reinterpret_cast<const uint4*>(w[r] + ((size_t)gl * CPG + kk) * 16);
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                const int8_t* xrow = xsm + (size_t)b * n;
+                if (KIND == 8) {
+                    const uint4 x = *reinterpret_cast<const uint4*>(xrow + 16 * c);
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        int t = dp4a_us(wv[r].x, x.x, d[r][b]);
+                        t = dp4a_us(wv[r].y, x.y, t);
+                        t = dp4a_us(wv[r].z, x.z, t);
+                        d[r][b] = dp4a_us(wv[r].w, x.w, t);
+                    }
+                } else {
+                    const uint4 xe = *reinterpret_cast<const uint4*>(xrow + 16 * c);
+                    const uint4 xo = *reinterpret_cast<const uint4*>(xrow + (n >> 1) + 16 * c);
+                    const uint32_t L4 = 0x0F0F0F0Fu, H4 = 0xF0F0F0F0u;
+#pragma unroll
+                    for (int r = 0; r < R; ++r) {
+                        const uint32_t a0 = wv[r].x ^ 0x88888888u, a1 = wv[r].y ^ 0x88888888u,
+                                       a2 = wv[r].z ^ 0x88888888u, a3 = wv[r].w ^ 0x88888888u;
+                        int dl = dp4a_us(a0 & L4, xe.x, 0);
+                        int dh = dp4a_us(a0 & H4, xo.x, 0);
+                        dl = dp4a_us(a1 & L4, xe.y, dl);
+                        dh = dp4a_us(a1 & H4, xo.y, dh);
+                        dl = dp4a_us(a2 & L4, xe.z, dl);
+                        dh = dp4a_us(a2 & H4, xo.z, dh);
+                        dl = dp4a_us(a3 & L4, xe.w, dl);
+                        dh = dp4a_us(a3 & H4, xo.w, dh);
+                        d[r][b] += dl + (dh >> 4);
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+            const float xsc = xs[b * ng + g];
+            const int xsu = BIAS * xsum[b * ng + g];
+#pragma unroll
+            for (int r = 0; r < R; ++r) acc[r][b] = fmaf(sc[r][gl] * xsc, (float)(d[r][b] - xsu), acc[r][b]);
+        }
+    }
+}
+
+template <int KIND, int NB, int CPG>
+__global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __grid_constant__ GemvArgs a, int prefetch) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    pdl_trigger();
+    const Layout L = make_layout(a);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.off_bars);
+    float* red = reinterpret_cast<float*>(smem + L.off_red);
+    int8_t* xsm = reinterpret_cast<int8_t*>(smem + L.off_x);
+    float* xs = reinterpret_cast<float*>(smem + L.off_xs);
+    int* xsum = reinterpret_cast<int*>(smem + L.off_xsum);
+    const int n = a.cols, ng = n / a.gs;
+    const int rb = KIND == 8 ? n : n / 2;
+    const int gb = KIND == 8 ? a.gs : a.gs / 2;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tw = a.paired ? kSlotW / 2 : kSlotW;  // weight bytes per tensor in a slot
+    int P = 0;
+    for (int i = 0; i < a.nseg; ++i) P += a.seg[i].rows >> 1;
+    const int nw = blockDim.x >> 5;
+    const long long W = (long long)gridDim.x * nw, wg = (long long)blockIdx.x * nw + warp;
+    TIter iss = {(int)(wg * P / W), (int)((wg + 1) * P / W), 0};
+    TIter cmp = iss;
+    uint64_t* bar = full + 2 * warp;
+    uint8_t* slots = smem + L.off_stage + (size_t)warp * 2 * L.stage_bytes;
+    uint64_t* tr = a.trace ? a.trace + (size_t)blockIdx.x * 4 : nullptr;
+    if (tr && threadIdx.x == 0) tr[0] = globaltimer();
+
+    if (lane == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+    }
+    fence_mbar_init();
+    __syncwarp();
+    uint64_t pol = 0;
+    TItem it;
+    if (lane == 0) {
+        pol = l2_evict_first_policy();
+        if (!prefetch) pdl_wait();
+        for (int s = 0; s < 2 && titem_next(a, iss, rb, it); ++s)
+            titem_issue(a, it, slots + (size_t)s * L.stage_bytes, &bar[s], rb, ng, gb, tw, pol);
+    }
+    pdl_wait();
+    if (tr && threadIdx.x == 0) tr[1] = globaltimer();
+    stage_input<KIND>(a, xsm, xs, xsum, red, threadIdx.x, blockDim.x);
+    __syncthreads();
+    if (tr && threadIdx.x == 0) tr[2] = globaltimer();
+    // every lane walks the issue iterator too (lane 0 already advanced it)
+    if (lane != 0)
+        for (int s = 0; s < 2 && titem_next(a, iss, rb, it); ++s) {
+        }
+
+    float acc[2][NB], acc2[2][NB];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) acc[0][b] = acc[1][b] = acc2[0][b] = acc2[1][b] = 0.0f;
+    for (int k = 0; titem_next(a, cmp, rb, it); ++k) {
+        const int s = k & 1;
+        if (!mbar_wait(&bar[s], (k >> 1) & 1, a.err, DEV_TIMEOUT_FULL)) {
+            // give up: confirm the copy of the other slot too, then leave
+            if (lane == 0) mbar_wait(&bar[s ^ 1], ((k + 1) >> 1) & 1, a.err, DEV_TIMEOUT_DRAIN);
+            return;
+        }
+        const uint8_t* sw = slots + (size_t)s * L.stage_bytes;
+        const float* ss = reinterpret_cast<const float*>(sw + kSlotW);
+        const GemvSeg& g = a.seg[it.seg];
+        if (!a.split) {
+            const float* ss2 = ss + it.nrows * ng;
+            for (int r = 0; r < it.nrows; r += 2) {
+                float v[4][NB];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                    for (int b = 0; b < NB; ++b) v[q][b] = 0.0f;
+                if (a.paired) {
+                    const uint8_t* wr[4] = {sw + (size_t)r * rb, sw + (size_t)(r + 1) * rb, sw + tw + (size_t)r * rb,
+                                            sw + tw + (size_t)(r + 1) * rb};
+                    const float* sr[4] = {ss + (size_t)r * ng, ss + (size_t)(r + 1) * ng, ss2 + (size_t)r * ng,
+                                          ss2 + (size_t)(r + 1) * ng};
+                    smem_rows_dot<KIND, NB, CPG, 4>(wr, sr, 0, ng, xsm, xs, xsum, n, ng, lane, v);
+                } else {
+                    const uint8_t* wr[2] = {sw + (size_t)r * rb, sw + (size_t)(r + 1) * rb};
+                    const float* sr[2] = {ss + (size_t)r * ng, ss + (size_t)(r + 1) * ng};
+                    smem_rows_dot<KIND, NB, CPG, 2>(wr, sr, 0, ng, xsm, xs, xsum, n, ng, lane, v);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                    for (int b = 0; b < NB; ++b) v[q][b] = warp_sum(v[q][b]);
+                if (lane == 0) {
+#pragma unroll
+                    for (int b = 0; b < NB; ++b) finish_rows(a, g, b, it.row + r, v[0][b], v[1][b], v[2][b], v[3][b], true);
+                }
+            }
+        } else {
+            const int g0 = it.boff / gb, ngs = it.bytes / gb;
+            const int mult = a.paired ? 2 : 1;
+            const int region = a.scap / (2 * mult);
+            const uint8_t* sb = reinterpret_cast<const uint8_t*>(ss);
+            float tmp[4][NB];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+#pragma unroll
+                for (int b = 0; b < NB; ++b) tmp[q][b] = 0.0f;
+            if (a.paired) {
+                const uint8_t* wr[4] = {sw, sw + tw / 2, sw + tw, sw + tw + tw / 2};
+                const float* sr[4] = {reinterpret_cast<const float*>(sb), reinterpret_cast<const float*>(sb + region),
+                                      reinterpret_cast<const float*>(sb + 2 * region),
+                                      reinterpret_cast<const float*>(sb + 3 * region)};
+                smem_rows_dot<KIND, NB, CPG, 4>(wr, sr, g0, ngs, xsm, xs, xsum, n, ng, lane, tmp);
+            } else {
+                const uint8_t* wr[2] = {sw, sw + tw / 2};
+                const float* sr[2] = {reinterpret_cast<const float*>(sb), reinterpret_cast<const float*>(sb + region)};
+                smem_rows_dot<KIND, NB, CPG, 2>(wr, sr, g0, ngs, xsm, xs, xsum, n, ng, lane, tmp);
+            }
+#pragma unroll
+            for (int b = 0; b < NB; ++b) {
+                acc[0][b] += tmp[0][b];
+                acc[1][b] += tmp[1][b];
+                acc2[0][b] += tmp[2][b];
+                acc2[1][b] += tmp[3][b];
+            }
+            if (it.last) {
+#pragma unroll
+                for (int b = 0; b < NB; ++b) {
+                    const float v0 = warp_sum(acc[0][b]), v1 = warp_sum(acc[1][b]);
+                    const float u0 = warp_sum(acc2[0][b]), u1 = warp_sum(acc2[1][b]);
+                    acc[0][b] = acc[1][b] = acc2[0][b] = acc2[1][b] = 0.0f;
+                    if (lane == 0) finish_rows(a, g, b, it.row, v0, v1, u0, u1, true);
+                }
+            }
+        }
+        // refill this slot with the warp's item k + 2
+        __syncwarp();
+        TItem nx;
+        const bool more = titem_next(a, iss, rb, nx);
+        if (lane == 0 && more) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            titem_issue(a, nx, slots + (size_t)s * L.stage_bytes, &bar[s], rb, ng, gb, tw, pol);
+        }
+    }
+    if (tr) {
+        __syncthreads();
+        if (threadIdx.x == 0) tr[3] = globaltimer();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// stand-alone activation quantization (one pass, many CTAs): each thread
+// takes 8 consecutive values, gs/8 lanes form a group; rmsnorm CTAs each
+// compute the full sum of squares in the same fixed order.
+
+constexpr int kAqThreads = 256;
+
+__global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_constant__ ActQuantArgs a) {
+    __shared__ float red[kAqThreads / 32];
+    pdl_trigger();
+    pdl_wait();
+    const int b = blockIdx.y, n = a.n, gs = a.gs, ng = n / gs;
+    const int ctid = threadIdx.x;
+    const float* src = a.x ? a.x + (size_t)b * n : nullptr;
+    if (a.mode == IN_RMSNORM_EMB) {
+        src = a.emb + (size_t)a.meta[2 * b] * n;
+        if (blockIdx.x == 0)
+            for (int i = ctid; i < n; i += kAqThreads) a.x_out[(size_t)b * n + i] = src[i];
+    }
+    const bool norm = a.mode == IN_RMSNORM || a.mode == IN_RMSNORM_EMB;
+    float inv = 1.0f;
+    if (norm) {
+        // rmsnorm sum of squares: thread t takes float4 chunks t, t+256, ...
+        constexpr int U = 4;
+        float ss = 0.0f;
+        for (int c0 = ctid; c0 < n / 4; c0 += U * kAqThreads) {
+            float4 v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const int c = c0 + u * kAqThreads;
+                v[u] = c < n / 4 ? reinterpret_cast<const float4*>(src)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                ss = fmaf(v[u].x, v[u].x, ss);
+                ss = fmaf(v[u].y, v[u].y, ss);
+                ss = fmaf(v[u].z, v[u].z, ss);
+                ss = fmaf(v[u].w, v[u].w, ss);
+            }
+        }
+        ss = warp_sum(ss);
+        if ((ctid & 31) == 0) red[ctid >> 5] = ss;
+        __syncthreads();
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kAqThreads / 32; ++w) t += red[w];
+        inv = 1.0f / sqrtf(t / (float)n + 1e-5f);
+    }
+    const int lpg = gs / 8;
+    const int task = blockIdx.x * kAqThreads + ctid;  // 8 values per task
+    const bool on = task < ng * lpg;
+    const int k0 = (on ? task : 0) * 8;
+    float v[8];
+    float amax = 0.0f;
+    if (on) {
+        const float4 a0 = *reinterpret_cast<const float4*>(src + k0);
+        const float4 a1 = *reinterpret_cast<const float4*>(src + k0 + 4);
+        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+        v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+        if (norm) {
+            const float4 w0 = *reinterpret_cast<const float4*>(a.rms_w + k0);
+            const float4 w1 = *reinterpret_cast<const float4*>(a.rms_w + k0 + 4);
+            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = w[i] * (inv * v[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+    for (int o = 1; o < lpg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float sc = amax / 127.0f;
+    if (sc == 0.0f) sc = 1e-8f;
+    const float rcp = 1.0f / sc;
+    int qs = 0;
+    if (on) {
+        int q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            q[i] = max(-127, min(127, quant_div(v[i], sc, rcp)));
+            qs += q[i];
+        }
+        const uint32_t lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+        const uint32_t hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+        *reinterpret_cast<uint2*>(a.xq + (size_t)b * n + k0) = make_uint2(lo, hi);
+    }
+    for (int o = 1; o < lpg; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+    if (on && (task & (lpg - 1)) == 0) {
+        const int g = task / lpg;
+        a.xs[(size_t)b * ng + g] = sc;
+        a.xsum[(size_t)b * ng + g] = qs;
+    }
+}
+
+cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl) {
+    if (!gs_ok_dev(a.gs) || a.n % a.gs || a.n % 8) return cudaErrorInvalidValue;
+    const int tasks = a.n / 8;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((tasks + kAqThreads - 1) / kAqThreads, a.nb);
+    cfg.blockDim = dim3(kAqThreads);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, act_quant_kernel, a);
+}
+
+// ---------------------------------------------------------------------------
 // host side
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-static bool gs_ok(int gs) { return gs == 32 || gs == 64 || gs == 128 || gs == 256; }
+static bool gs_ok(int gs) { return gs_ok_dev(gs); }
 
 bool gemv_args_ok(const GemvArgs& a, int kind) {
     if (!gs_ok(a.gs) || a.cols % a.gs || a.nseg < 1 || a.nseg > kMaxSegs) return false;
+    // the rmsnorm prologue holds the whole input in registers: 8 values x 8 rounds x 256 threads
+    if ((a.in_mode == IN_RMSNORM || a.in_mode == IN_RMSNORM_EMB) && a.cols > 8 * 8 * kCT) return false;
     for (int i = 0; i < a.nseg; ++i) {
         if (!aligned16(a.seg[i].wq)) return false;
         if (a.paired && !aligned16(a.seg[i].wq2)) return false;
@@ -523,8 +1007,86 @@ bool gemv_args_ok(const GemvArgs& a, int kind) {
     return true;
 }
 
+static bool tma_ok(const GemvArgs& a) {
+    if ((a.cols / a.gs) % 4) return false;
+    for (int i = 0; i < a.nseg; ++i) {
+        if (a.seg[i].rows % 2) return false;
+        if (!aligned16(a.seg[i].wq) || !aligned16(a.seg[i].ws)) return false;
+        if (a.paired && (!aligned16(a.seg[i].wq2) || !aligned16(a.seg[i].ws2))) return false;
+    }
+    return true;
+}
+
+static int g_use_tma = -1;
+
+template <int KIND, int NB, int CPG>
+static cudaError_t launch_tma(GemvArgs a, cudaStream_t st, bool pdl, int num_sms) {
+    const int rb = KIND == 8 ? a.cols : a.cols / 2;
+    const int gb = KIND == 8 ? a.gs : a.gs / 2;
+    const int ng = a.cols / a.gs;
+    const int mult = a.paired ? 2 : 1;
+    const int tw = kSlotW / mult;
+    a.x_bytes = align_up(a.nb * a.cols, 16);
+    a.wcap = kSlotW;
+    if (2 * rb <= tw) {
+        a.split = 0;
+        a.stage_rows = 2 * (tw / (2 * rb));
+        a.slice_bytes = 0;
+        a.scap = align_up(mult * a.stage_rows * ng * 4, 128);
+    } else {
+        a.split = 1;
+        a.stage_rows = 2;
+        a.slice_bytes = tw / 2;
+        a.scap = align_up(2 * mult * align_up(a.slice_bytes / gb * 4, 16), 128);
+    }
+    int P = 0;
+    for (int i = 0; i < a.nseg; ++i) P += a.seg[i].rows / 2;
+    if (P == 0) return cudaSuccess;
+    // as many warps (two slots each) as shared memory holds, up to 16
+    int nw = 0;
+    for (int w = kTmaMaxWarps; w >= 4 && !nw; w -= 2) {
+        a.nstages = 2 * w;
+        if (make_layout(a).total <= 227 * 1024) nw = w;
+    }
+    if (!nw) return cudaErrorInvalidValue;
+    a.nstages = 2 * nw;
+    const Layout L = make_layout(a);
+    auto kern = gemv_tma_kernel<KIND, NB, CPG>;
+    static int set_bytes = 0;
+    if (L.total > set_bytes) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        if (e != cudaSuccess) return e;
+        set_bytes = 227 * 1024;
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    int grid = (P + nw - 1) / nw;
+    if (grid > num_sms) grid = num_sms;
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(nw * 32);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, a, pdl ? 1 : 0);
+}
+
 template <int KIND, int NB, int CPG>
 static cudaError_t launch_cpg(GemvArgs a, cudaStream_t st, bool pdl, int num_sms, int ctas_per_sm) {
+    if (g_use_tma < 0) {
+        const char* e = getenv("LQ_GEMV_TMA");
+        g_use_tma = e ? atoi(e) : 1;
+    }
+    if (g_use_tma && tma_ok(a)) {
+        const int rb = KIND == 8 ? a.cols : a.cols / 2;
+        (void)rb;
+        GemvArgs t = a;
+        t.x_bytes = align_up(a.nb * a.cols, 16);
+        if (make_layout(t).off_stage + 2 * 4 * (kSlotW + 4096) <= 227 * 1024)
+            return launch_tma<KIND, NB, CPG>(a, st, pdl, num_sms);
+    }
     a.x_bytes = align_up(a.nb * a.cols, 16);
     a.nstages = 0;
     a.wcap = a.scap = 0;

@@ -1,7 +1,10 @@
 // Per-device context shared by the C-ABI sources (C++ only).
 #pragma once
 #include <cstddef>
+#include <cstdint>
 #include <cuda_runtime.h>
+
+#include "lq_host.h"
 
 namespace lq {
 
@@ -18,5 +21,7 @@ int ensure_scratch(DevCtx* c, size_t bytes);
 int cuda_fail(cudaError_t e, const char* what);
 int check_device_error(int* err_dev, cudaStream_t st);
 cudaStream_t stream();
+int matmul_f32_device(float* yd, const float* xd, const QuantizedTensor* w, int n, int d, int8_t* xq, float* xs,
+                      int* xsum, int* err, cudaStream_t st, bool pdl_first, int num_sms, uint64_t* trace);
 
 }  // namespace lq

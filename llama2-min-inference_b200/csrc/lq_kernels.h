@@ -48,6 +48,7 @@ struct GemvArgs {
     int in_mode;
     const int8_t* xq;  // IN_QUANT [nb, cols]
     const float* xs;   // IN_QUANT [nb, cols/gs]
+    const int* xsum_in;  // IN_QUANT, optional: group sums of xq [nb, cols/gs] (computed when null)
     const float* xf;   // fp32 source [nb, cols] (IN_F32, IN_RMSNORM)
     const float* rms_w;
     const float* emb;  // IN_RMSNORM_EMB table [vocab, cols]
@@ -61,6 +62,7 @@ struct GemvArgs {
     int max_seq;
     int64_t kv_seq_stride;  // elements between sequences' caches
     int* err;
+    uint64_t* trace;  // optional per-CTA phase timestamps (globaltimer ns), [grid][4]; null = off
     // schedule (filled by the planner)
     int split;       // 0: stages of whole rows; 1: stages are slices of one row
     int stage_rows;  // rows per stage (whole-row mode)
@@ -70,6 +72,23 @@ struct GemvArgs {
     int x_bytes;     // shared-memory bytes for the staged activation
     int paired;      // segments carry a second tensor (EPI_SWIGLU)
 };
+
+// Activation quantization kernel (quantize_act, v1-int8-vnni/runq.c:117-139,
+// optionally after rmsnorm, runq.c:294-305): writes int8 xq [nb, n] in
+// natural order, fp32 scales xs and int32 group sums xsum [nb, n/gs].
+struct ActQuantArgs {
+    int mode;          // IN_F32, IN_RMSNORM or IN_RMSNORM_EMB
+    int n, gs, nb;
+    const float* x;    // [nb, n] (IN_F32 / IN_RMSNORM)
+    const float* rms_w;
+    const float* emb;  // IN_RMSNORM_EMB: x = emb[meta[2b]]
+    const int* meta;
+    float* x_out;      // IN_RMSNORM_EMB: copy of the embedding row (residual stream)
+    int8_t* xq;
+    float* xs;
+    int* xsum;
+};
+cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl);
 
 // Plan and launch.  pdl: allow programmatic dependent launch overlap with
 // the previous kernel on the stream.  Returns a cudaError_t.

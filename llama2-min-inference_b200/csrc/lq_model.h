@@ -31,6 +31,9 @@ struct Transformer {
     lq::QW wq, wk, wv, wo, w1, w2, w3, wcls;
     // activations and caches (device); leading dimension max_batch
     float *x = nullptr, *q = nullptr, *att = nullptr, *h1 = nullptr, *h3 = nullptr, *logits = nullptr;
+    int8_t* xq = nullptr;  // quantized activation feeding the next GEMV
+    float* xqs = nullptr;
+    int* xqsum = nullptr;
     float *kc = nullptr, *vc = nullptr;  // [B][L][kv_heads][max_seq][head_size]
     float* part = nullptr;               // attention partials
     int* counters = nullptr;             // attention arrival counters

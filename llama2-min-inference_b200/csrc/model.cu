@@ -1,14 +1,16 @@
 // Transformer: checkpoint upload / on-device random init, and the decode
 // step captured as one CUDA graph.
 //
-// Per layer the step is five kernels (reference order, runq.c:335-415):
-//   1. GEMV [wq|wk|wv]   prologue rmsnorm(x)+quantize (layer 0: x = emb[token])
-//                        epilogue RoPE(q) -> q, RoPE(k) -> K cache, v -> V cache
-//   2. attention         split-KV over the cache, normalised fp32 output
-//   3. GEMV wo           prologue quantize(att), epilogue x += .
-//   4. GEMV [w1|w3]      prologue rmsnorm(x)+quantize, epilogue h = silu(w1 x) * (w3 x)
-//   5. GEMV w2           prologue quantize(h), epilogue x += .
-// then GEMV wcls (prologue final rmsnorm + quantize) and argmax.  Every
+// Per layer the step is nine kernels (reference order, runq.c:335-415):
+//   quantize(rmsnorm(x))  (layer 0: x = emb[token])
+//   GEMV [wq|wk|wv]       epilogue RoPE(q) -> q, RoPE(k) -> K cache, v -> V cache
+//   attention             split-KV over the cache, normalised fp32 output
+//   quantize(att), GEMV wo            epilogue x += .
+//   quantize(rmsnorm(x)), GEMV [w1|w3] epilogue h = silu(w1 x) * (w3 x)
+//   quantize(h), GEMV w2              epilogue x += .
+// then quantize(rmsnorm(x)), GEMV wcls and argmax.  The quantizers are
+// wide one-pass kernels that also emit the int32 group sums the GEMV needs;
+// every GEMV streams its weights from kernel start.  Every
 // kernel is launched with programmatic dependent launch, so each GEMV's
 // weight stream starts while its predecessor is finishing.  The graph reads
 // token and position from device memory (the reference's d_meta idea,
@@ -99,6 +101,10 @@ int alloc_state(Transformer* t) {
     rc = rc ? rc : dalloc(&t->h1, (size_t)B * c.hidden_dim);
     rc = rc ? rc : dalloc(&t->h3, (size_t)B * c.hidden_dim);
     rc = rc ? rc : dalloc(&t->logits, (size_t)B * c.vocab_size);
+    const int maxn = c.hidden_dim > c.dim ? c.hidden_dim : c.dim;
+    rc = rc ? rc : dalloc(&t->xq, (size_t)B * maxn);
+    rc = rc ? rc : dalloc(&t->xqs, (size_t)B * (maxn / t->gs));
+    rc = rc ? rc : dalloc(&t->xqsum, (size_t)B * (maxn / t->gs));
     rc = rc ? rc : dalloc(&t->kc, kv);
     rc = rc ? rc : dalloc(&t->vc, kv);
     rc = rc ? rc : dalloc(&t->part, (size_t)B * c.n_heads * t->max_splits * (t->head_size + 2));
@@ -160,19 +166,40 @@ int forward_launch(Transformer* t, int batch) {
         a.err = t->err;
     };
     cudaError_t e;
+    // activation quantizer in front of every GEMV (quantize_act, runq.c:345,394,400,412,418)
+    auto quant = [&](int mode, const float* x, int n, const float* rms_w) -> cudaError_t {
+        ActQuantArgs q{};
+        q.mode = mode;
+        q.n = n;
+        q.gs = gs;
+        q.nb = batch;
+        q.x = x;
+        q.rms_w = rms_w;
+        q.emb = t->emb;
+        q.meta = t->meta;
+        q.x_out = t->x;
+        q.xq = t->xq;
+        q.xs = t->xqs;
+        q.xsum = t->xqsum;
+        return act_quant_launch(q, st, true);
+    };
+    auto qin = [&](GemvArgs& a) {
+        a.in_mode = IN_QUANT;
+        a.xq = t->xq;
+        a.xs = t->xqs;
+        a.xsum_in = t->xqsum;
+    };
     for (int l = 0; l < c.n_layers; ++l) {
         GemvArgs a;
-        // 1. q, k, v
+        // 1. q, k, v (attention rmsnorm + quantize first; layer 0 starts from emb[token])
+        if ((e = quant(l == 0 ? IN_RMSNORM_EMB : IN_RMSNORM, t->x, D, t->rms_att + (size_t)l * D)) != cudaSuccess)
+            return cuda_fail(e, "attention rmsnorm");
         base(a, D);
         a.seg[0] = {t->wq.q + (size_t)l * D * rbD, t->wq.s + (size_t)l * D * ngD, t->q, D, EPI_ROPE_Q};
         a.seg[1] = {t->wk.q + (size_t)l * KV * rbD, t->wk.s + (size_t)l * KV * ngD, nullptr, KV, EPI_ROPE_KCACHE};
         a.seg[2] = {t->wv.q + (size_t)l * KV * rbD, t->wv.s + (size_t)l * KV * ngD, nullptr, KV, EPI_VCACHE};
         a.nseg = 3;
-        a.in_mode = l == 0 ? IN_RMSNORM_EMB : IN_RMSNORM;
-        a.xf = t->x;
-        a.rms_w = t->rms_att + (size_t)l * D;
-        a.emb = t->emb;
-        a.x_out = t->x;
+        qin(a);
         a.kcache = t->kc + l * kv_layer;
         a.vcache = t->vc + l * kv_layer;
         if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
@@ -195,46 +222,45 @@ int forward_launch(Transformer* t, int batch) {
         at.max_splits = t->max_splits;
         if ((e = attention_launch(at, batch, st, true)) != cudaSuccess) return cuda_fail(e, "attention");
         // 3. wo + residual
+        if ((e = quant(IN_F32, t->att, D, nullptr)) != cudaSuccess) return cuda_fail(e, "attention output quantize");
         base(a, D);
         a.seg[0] = {t->wo.q + (size_t)l * D * rbD, t->wo.s + (size_t)l * D * ngD, t->x, D, EPI_ADD};
         a.nseg = 1;
-        a.in_mode = IN_F32;
-        a.xf = t->att;
+        qin(a);
         if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "wo gemv");
         // 4. w1 | w3 paired, SwiGLU in the epilogue: h1 = silu(x.w1) * (x.w3)
+        if ((e = quant(IN_RMSNORM, t->x, D, t->rms_ffn + (size_t)l * D)) != cudaSuccess)
+            return cuda_fail(e, "ffn rmsnorm");
         base(a, D);
         a.seg[0] = {t->w1.q + (size_t)l * H * rbD, t->w1.s + (size_t)l * H * ngD, t->h1, H, EPI_SWIGLU,
                     t->w3.q + (size_t)l * H * rbD, t->w3.s + (size_t)l * H * ngD};
         a.nseg = 1;
         a.paired = 1;
         a.y_stride = H;
-        a.in_mode = IN_RMSNORM;
-        a.xf = t->x;
-        a.rms_w = t->rms_ffn + (size_t)l * D;
+        qin(a);
         if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w1/w3 gemv");
         // 5. w2 + residual
+        if ((e = quant(IN_F32, t->h1, H, nullptr)) != cudaSuccess) return cuda_fail(e, "ffn quantize");
         base(a, H);
         a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->x, D, EPI_ADD};
         a.nseg = 1;
-        a.in_mode = IN_F32;
-        a.xf = t->h1;
+        qin(a);
         if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
     }
     GemvArgs a;
+    if ((e = quant(IN_RMSNORM, t->x, D, t->rms_final)) != cudaSuccess) return cuda_fail(e, "final rmsnorm");
     base(a, D);
     a.seg[0] = {t->wcls.q, t->wcls.s, t->logits, c.vocab_size, EPI_STORE};
     a.nseg = 1;
     a.y_stride = c.vocab_size;
-    a.in_mode = IN_RMSNORM;
-    a.xf = t->x;
-    a.rms_w = t->rms_final;
+    qin(a);
     if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "classifier gemv");
     if ((e = argmax_launch(t->logits, c.vocab_size, batch, c.vocab_size, t->next, st, true)) != cudaSuccess)
         return cuda_fail(e, "argmax");
     return LQ_OK;
 }
 
-int kernels_per_step(const Transformer* t) { return 5 * t->c.n_layers + 2; }
+int kernels_per_step(const Transformer* t) { return 9 * t->c.n_layers + 3; }
 
 static int ensure_graph(Transformer* t, int batch) {
     if (t->exec && t->graph_batch == batch) return LQ_OK;
@@ -447,7 +473,7 @@ void free_transformer(Transformer* t) {
         cudaFree(w->q);
         cudaFree(w->s);
     }
-    void* bufs[] = {t->emb, t->rms_att, t->rms_ffn, t->rms_final, t->x, t->q, t->att, t->h1, t->h3,
+    void* bufs[] = {t->emb, t->rms_att, t->rms_ffn, t->rms_final, t->x, t->q, t->att, t->h1, t->h3, t->xq, t->xqs, t->xqsum,
                     t->logits, t->kc, t->vc, t->part, t->counters, t->meta, t->next, t->err};
     for (void* b : bufs) cudaFree(b);
     cudaFreeHost(t->h_logits);
