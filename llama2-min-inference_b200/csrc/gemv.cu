@@ -356,15 +356,15 @@ __device__ __forceinline__ void block_dot(const uint8_t* const* rows, const floa
 // ---------------------------------------------------------------------------
 // epilogue
 
-__device__ __forceinline__ void rope_pair(float& v0, float& v1, int r, int head_size, int pos) {
-    // RoPE, v1-int8-vnni/runq.c:351-365
-    const int hd = r % head_size;
-    const float freq = 1.0f / powf(10000.0f, hd / (float)head_size);
-    const float val = pos * freq;
-    const float fcr = cosf(val), fci = sinf(val);
+// RoPE, v1-int8-vnni/runq.c:351-365.  cos/sin of pos * freq come from a
+// table the host fills with the reference's own formula (1/powf(10000,
+// hd/hs), cosf, sinf), so the rotation needs no device transcendentals and
+// matches the CPU bit for bit.
+__device__ __forceinline__ void rope_pair(const float2* rope, float& v0, float& v1, int r, int head_size, int pos) {
+    const float2 cs = rope[(size_t)pos * (head_size >> 1) + ((r % head_size) >> 1)];
     const float a0 = v0, a1 = v1;
-    v0 = a0 * fcr - a1 * fci;
-    v1 = a0 * fci + a1 * fcr;
+    v0 = a0 * cs.x - a1 * cs.y;
+    v1 = a0 * cs.y + a1 * cs.x;
 }
 
 // Finish rows r and r+1 (when has2) of segment g for batch row b.  For
@@ -389,14 +389,14 @@ __device__ void finish_rows(const GemvArgs& a, const GemvSeg& g, int b, int r, f
             if (has2) y[r + 1] = lq_swiglu(v1, u1);
         } break;
         case EPI_ROPE_Q: {
-            rope_pair(v0, v1, r, a.head_size, pos);
+            rope_pair(a.rope, v0, v1, r, a.head_size, pos);
             float* y = g.y + (size_t)b * a.y_stride;
             y[r] = v0;
             y[r + 1] = v1;
         } break;
         case EPI_ROPE_KCACHE:
         case EPI_VCACHE: {
-            if (g.epi == EPI_ROPE_KCACHE) rope_pair(v0, v1, r, a.head_size, pos);
+            if (g.epi == EPI_ROPE_KCACHE) rope_pair(a.rope, v0, v1, r, a.head_size, pos);
             float* c = (g.epi == EPI_ROPE_KCACHE ? a.kcache : a.vcache) + (size_t)b * a.kv_seq_stride;
             const int hs = a.head_size;
             const size_t o = ((size_t)(r / hs) * a.max_seq + pos) * hs + (r % hs);

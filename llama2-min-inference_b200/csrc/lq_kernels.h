@@ -56,6 +56,7 @@ struct GemvArgs {
     int y_stride;      // elements between batch rows of y (EPI_STORE / EPI_ADD)
     // decode state
     const int* meta;   // per batch row: [token, pos]
+    const float2* rope;  // [max_seq][head_size/2] (cos, sin) of pos * freq
     int head_size;
     float* kcache;     // layer base, [kv_heads][max_seq][head_size] per sequence
     float* vcache;

@@ -40,6 +40,7 @@ struct Transformer {
     int* meta = nullptr;                 // [B][token, pos]
     int* next = nullptr;                 // [B] argmax
     int* err = nullptr;                  // device error word
+    float2* rope = nullptr;              // [max_seq][head_size/2] cos/sin table
     // pinned host mirrors
     float* h_logits = nullptr;
     int *h_meta = nullptr, *h_next = nullptr, *h_err = nullptr;

@@ -22,6 +22,7 @@
 
 #include <cstdio>
 #include <cstdlib>
+#include <cmath>
 #include <cstring>
 #include <vector>
 
@@ -112,7 +113,21 @@ int alloc_state(Transformer* t) {
     rc = rc ? rc : dalloc(&t->meta, (size_t)2 * B);
     rc = rc ? rc : dalloc(&t->next, (size_t)B);
     rc = rc ? rc : dalloc(&t->err, 1);
+    rc = rc ? rc : dalloc(&t->rope, (size_t)t->max_seq * (t->head_size / 2));
     if (rc) return rc;
+    {
+        // RoPE table with the reference's arithmetic (runq.c:352-356)
+        const int hs = t->head_size;
+        std::vector<float2> tab((size_t)t->max_seq * (hs / 2));
+        for (int pos = 0; pos < t->max_seq; ++pos)
+            for (int i = 0; i < hs / 2; ++i) {
+                const float freq = 1.0f / powf(10000.0f, (2 * i) / (float)hs);
+                const float val = pos * freq;
+                tab[(size_t)pos * (hs / 2) + i] = make_float2(cosf(val), sinf(val));
+            }
+        cudaError_t e0 = cudaMemcpy(t->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice);
+        if (e0 != cudaSuccess) return cuda_fail(e0, "rope table");
+    }
     cudaError_t e = cudaMemset(t->counters, 0, (size_t)B * c.n_kv_heads * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(t->err, 0, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(t->meta, 0, 2 * B * sizeof(int));
@@ -160,6 +175,7 @@ int forward_launch(Transformer* t, int batch) {
         a.nb = batch;
         a.y_stride = D;
         a.meta = t->meta;
+        a.rope = t->rope;
         a.head_size = hs;
         a.max_seq = t->max_seq;
         a.kv_seq_stride = kv_seq;
@@ -474,7 +490,7 @@ void free_transformer(Transformer* t) {
         cudaFree(w->s);
     }
     void* bufs[] = {t->emb, t->rms_att, t->rms_ffn, t->rms_final, t->x, t->q, t->att, t->h1, t->h3, t->xq, t->xqs, t->xqsum,
-                    t->logits, t->kc, t->vc, t->part, t->counters, t->meta, t->next, t->err};
+                    t->logits, t->kc, t->vc, t->part, t->counters, t->meta, t->next, t->err, t->rope};
     for (void* b : bufs) cudaFree(b);
     cudaFreeHost(t->h_logits);
     cudaFreeHost(t->h_meta);

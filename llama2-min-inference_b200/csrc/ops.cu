@@ -4,6 +4,7 @@
 #include <cfloat>
 
 #include "lq_device.cuh"
+#include "lq_math.h"
 #include "lq_ops.h"
 
 namespace lq {
@@ -95,7 +96,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         for (int j = 0; j < km; ++j) {
             const float* qj = qs + j * hs;
             float p = 0.0f;
-            for (int i = lane; i < hs; i += 32) p += qj[i] * kt[i];
+            for (int i = lane; i < hs; i += 32) p = fmaf(qj[i], kt[i], p);
             p = warp_sum(p);
             if (lane == 0) sc[j * kChunk + t] = p / rs;
         }
@@ -108,7 +109,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         m = warp_max(m);
         float l = 0.0f;
         for (int t = lane; t < nt; t += 32) {
-            const float e = expf(sc[j * kChunk + t] - m);
+            const float e = lq_expf(sc[j * kChunk + t] - m);
             sc[j * kChunk + t] = e;
             l += e;
         }
@@ -126,7 +127,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         const int j = i / hs, d = i - j * hs;
         const float* pj = sc + j * kChunk;
         float o = 0.0f;
-        for (int t = 0; t < nt; ++t) o += pj[t] * vs[t * hs + d];
+        for (int t = 0; t < nt; ++t) o = fmaf(pj[t], vs[t * hs + d], o);
         if (nsplit == 1) {
             out[i] = o / ml[2 * j + 1];
         } else {
@@ -159,9 +160,9 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         float L = 0.0f, o = 0.0f;
         for (int s = 0; s < nsplit; ++s) {
             const float* ps = base + (size_t)s * (hs + 2);
-            const float w = expf(__ldcg(ps) - M);
-            L += __ldcg(ps + 1) * w;
-            o += __ldcg(ps + 2 + d) * w;
+            const float w = lq_expf(__ldcg(ps) - M);
+            L = fmaf(__ldcg(ps + 1), w, L);
+            o = fmaf(__ldcg(ps + 2 + d), w, o);
         }
         out[i] = o / L;
     }

@@ -398,3 +398,258 @@ int orc_argmax(const float* v, int n) {                            /* runq.c:578
     for (int i = 1; i < n; i++) if (v[i] > mv) { mi = i; mv = v[i]; }
     return mi;
 }
+
+
+/* ======================================================================== */
+/* Kernel-order forward                                                      */
+/*                                                                           */
+/* The same decode step as orc_forward, with every floating-point reduction  */
+/* evaluated in the order the B200 kernels of the product use, so that the   */
+/* product's logits can be compared bit for bit.  The math is runq.c's       */
+/* (file:line cited at each step); only the association order of the fp32    */
+/* sums differs from runq.c, as it must for any parallel implementation:     */
+/*  - a 32-lane warp sum is the xor butterfly (lane l adds lane l^16, l^8,   */
+/*    l^4, l^2, l^1 in turn);                                                */
+/*  - GEMV rows: lane L accumulates fmaf((ws*xs), D, acc) over its groups;   */
+/*    which groups a lane owns depends on the kernel that runs the shape;    */
+/*  - rmsnorm: 256 threads, thread t sums float4 chunks t, t+256, ...;       */
+/*  - attention in chunks of 64 positions merged with max / exp weights;     */
+/*  - exp is the project's own Cody-Waite + degree-7 Taylor evaluation and   */
+/*    RoPE cos/sin come from a table built with runq.c's formula.            */
+/* ======================================================================== */
+
+static float pow2i(int k) {
+    unsigned u = (unsigned)(k + 127) << 23;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* exp(x): x = k ln2 + r, |r| <= ln2/2, Taylor degree 7 (same constants and
+ * operation order as the product's device code). */
+float orc_expf(float x) {
+    if (!(x > -104.0f)) return x != x ? x : 0.0f;
+    if (x > 88.75f) return pow2i(127) * 2.0f;
+    const float k = rintf(x * 1.44269502f);
+    float r = fmaf(k, -0.693145751953125f, x);
+    r = fmaf(k, -1.42860677e-06f, r);
+    float p = 1.98412698e-04f;
+    p = fmaf(p, r, 1.38888889e-03f);
+    p = fmaf(p, r, 8.33333377e-03f);
+    p = fmaf(p, r, 4.16666679e-02f);
+    p = fmaf(p, r, 1.66666672e-01f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int ki = (int)k;
+    if (ki > 127) return p * pow2i(127) * pow2i(ki - 127);
+    if (ki < -126) return p * pow2i(ki + 64) * pow2i(-64);
+    return p * pow2i(ki);
+}
+
+static float warp_butterfly(float* v) { /* 32 values, returns lane 0's result */
+    for (int o = 16; o > 0; o >>= 1) {
+        float nv[32];
+        for (int l = 0; l < 32; l++) nv[l] = v[l] + v[l ^ o];
+        memcpy(v, nv, sizeof(nv));
+    }
+    return v[0];
+}
+
+/* rmsnorm + quantize as the product's activation quantizer */
+static void mirror_act_quant(const float* x, const float* w, int n, int gs, int8_t* xq, float* xs, float* tmp) {
+    if (w) {
+        float red[8];
+        for (int wi = 0; wi < 8; wi++) {
+            float lanes[32];
+            for (int l = 0; l < 32; l++) {
+                int t = wi * 32 + l;
+                float ss = 0.0f;
+                for (int c = t; c < n / 4; c += 256)
+                    for (int e = 0; e < 4; e++) ss = fmaf(x[4 * c + e], x[4 * c + e], ss);
+                lanes[l] = ss;
+            }
+            red[wi] = warp_butterfly(lanes);
+        }
+        float t = 0.0f;
+        for (int wi = 0; wi < 8; wi++) t += red[wi];
+        float inv = 1.0f / sqrtf(t / (float)n + 1e-5f);
+        for (int i = 0; i < n; i++) tmp[i] = w[i] * (inv * x[i]);
+        x = tmp;
+    }
+    orc_quantize_act(x, n, gs, xq, xs, NULL);
+}
+
+/* kernel selection of the product's GEMV (bulk-copy kernel when every
+ * segment has an even row count and the group count is a multiple of 4) */
+typedef struct {
+    int mode; /* 0: whole rows (bulk copy), 1: row slices (bulk copy), 2: plain-load kernel */
+    int slice_groups;
+    int lpg;  /* plain-load kernel: lanes per group */
+} RowOrder;
+
+static RowOrder row_order(int n, int gs, int kind, int paired, int rows_even) {
+    RowOrder o = {0, 0, 1};
+    int ng = n / gs, rb = kind == 8 ? n : n / 2, gb = kind == 8 ? gs : gs / 2;
+    if (ng % 4 == 0 && rows_even) {
+        int tw = 8192 / (paired ? 2 : 1);
+        if (2 * rb <= tw) o.mode = 0;
+        else { o.mode = 1; o.slice_groups = (tw / 2) / gb; }
+    } else {
+        int cpg = gb / 16;
+        o.mode = 2;
+        o.lpg = cpg == 1 ? 1 : 2;
+    }
+    return o;
+}
+
+static float mirror_row(const uint8_t* wrow, const float* srow, const int8_t* xq, const float* xs, int n, int gs,
+                        int kind, RowOrder o) {
+    int ng = n / gs;
+    float lanes[32] = {0};
+    float tmp[32];
+    for (int g = 0; g < ng; g++) {
+        int32_t d = 0;
+        for (int j = 0; j < gs; j++) d += wval(wrow, (int64_t)g * gs + j, kind) * (int32_t)xq[g * gs + j];
+        float f = srow[g] * xs[g];
+        if (o.mode == 0) {
+            lanes[g % 32] = fmaf(f, (float)d, lanes[g % 32]);
+        } else if (o.mode == 2) {
+            int lane = o.lpg == 1 ? g % 32 : 2 * (g % 16);
+            lanes[lane] = fmaf(f, (float)d, lanes[lane]);
+        } else {
+            int j = g / o.slice_groups, gl = g - j * o.slice_groups;
+            if (gl == 0) memset(tmp, 0, sizeof(tmp));
+            tmp[gl % 32] = fmaf(f, (float)d, tmp[gl % 32]);
+            if (gl == o.slice_groups - 1 || g == ng - 1)
+                for (int l = 0; l < 32; l++) lanes[l] = lanes[l] + tmp[l];
+        }
+    }
+    return warp_butterfly(lanes);
+}
+
+static void mirror_gemv(float* out, const OrcQ* w, int64_t l, int64_t rows, const int8_t* xq, const float* xs, int n,
+                        int gs, int kind, RowOrder o) {
+    size_t rb = row_bytes(n, kind);
+    const uint8_t* q = w->q + (size_t)l * rows * rb;
+    const float* s = w->s + (size_t)l * rows * (n / gs);
+    for (int64_t r = 0; r < rows; r++) out[r] = mirror_row(q + r * rb, s + r * (n / gs), xq, xs, n, gs, kind, o);
+}
+
+/* attention of one head over positions 0..pos in chunks of 64 (kernel order) */
+static void mirror_attention(const float* q, const float* kc, const float* vc, size_t stride, int pos, int hs,
+                             float* out) {
+    enum { CH = 64 };
+    int nsplit = pos / CH + 1;
+    float* part_m = (float*)malloc(sizeof(float) * nsplit);
+    float* part_l = (float*)malloc(sizeof(float) * nsplit);
+    float* part_o = (float*)malloc(sizeof(float) * nsplit * hs);
+    float rs = sqrtf((float)hs);
+    float sc[CH];
+    for (int s = 0; s < nsplit; s++) {
+        int t0 = s * CH, nt = pos + 1 - t0 < CH ? pos + 1 - t0 : CH;
+        for (int t = 0; t < nt; t++) {
+            const float* k = kc + (size_t)(t0 + t) * stride;
+            float lanes[32];
+            for (int l = 0; l < 32; l++) {
+                float p = 0.0f;
+                for (int i = l; i < hs; i += 32) p = fmaf(q[i], k[i], p);
+                lanes[l] = p;
+            }
+            sc[t] = warp_butterfly(lanes) / rs;
+        }
+        float m = -3.402823466e+38f;
+        for (int t = 0; t < nt; t++) m = fmaxf(m, sc[t]);
+        float lanes[32] = {0};
+        for (int t = 0; t < nt; t++) {
+            float e = orc_expf(sc[t] - m);
+            sc[t] = e;
+            lanes[t % 32] += e;
+        }
+        float lsum = warp_butterfly(lanes);
+        for (int d = 0; d < hs; d++) {
+            float o = 0.0f;
+            for (int t = 0; t < nt; t++) o = fmaf(sc[t], vc[(size_t)(t0 + t) * stride + d], o);
+            part_o[s * hs + d] = o;
+        }
+        part_m[s] = m;
+        part_l[s] = lsum;
+    }
+    if (nsplit == 1) {
+        for (int d = 0; d < hs; d++) out[d] = part_o[d] / part_l[0];
+    } else {
+        float M = -3.402823466e+38f;
+        for (int s = 0; s < nsplit; s++) M = fmaxf(M, part_m[s]);
+        for (int d = 0; d < hs; d++) {
+            float L = 0.0f, o = 0.0f;
+            for (int s = 0; s < nsplit; s++) {
+                float w = orc_expf(part_m[s] - M);
+                L = fmaf(part_l[s], w, L);
+                o = fmaf(part_o[s * hs + d], w, o);
+            }
+            out[d] = o / L;
+        }
+    }
+    free(part_m);
+    free(part_l);
+    free(part_o);
+}
+
+float* orc_forward_kernel_order(OrcModel* m, int token, int pos) {
+    OrcConfig* p = &m->c;
+    int dim = p->dim, hidden = p->hidden_dim, hs = dim / p->n_heads;
+    int kv_dim = dim * p->n_kv_heads / p->n_heads, kv_mul = p->n_heads / p->n_kv_heads;
+    int gs = m->gs, kind = m->kind;
+    float* x = m->x;
+    float* tmp = (float*)malloc(sizeof(float) * (hidden > dim ? hidden : dim));
+    memcpy(x, m->emb + (size_t)token * dim, dim * 4);
+    int qkv_even = dim % 2 == 0 && kv_dim % 2 == 0;
+    RowOrder o_dim = row_order(dim, gs, kind, 0, qkv_even);
+    RowOrder o_wo = row_order(dim, gs, kind, 0, dim % 2 == 0);
+    RowOrder o_ffn = row_order(dim, gs, kind, 1, hidden % 2 == 0);
+    RowOrder o_w2 = row_order(hidden, gs, kind, 0, dim % 2 == 0);
+    RowOrder o_cls = row_order(dim, gs, kind, 0, p->vocab_size % 2 == 0);
+    for (int64_t l = 0; l < p->n_layers; l++) {
+        size_t loff = (size_t)l * m->max_seq * kv_dim;
+        float* k = m->kc + loff + (size_t)pos * kv_dim;
+        float* v = m->vc + loff + (size_t)pos * kv_dim;
+        mirror_act_quant(x, m->rms_att + l * dim, dim, gs, m->aq, m->as, tmp);    /* runq.c:338,345 */
+        mirror_gemv(m->q, &m->wq, l, dim, m->aq, m->as, dim, gs, kind, o_dim);      /* :346-348 */
+        mirror_gemv(k, &m->wk, l, kv_dim, m->aq, m->as, dim, gs, kind, o_dim);
+        mirror_gemv(v, &m->wv, l, kv_dim, m->aq, m->as, dim, gs, kind, o_dim);
+        for (int i = 0; i < dim; i += 2) {                                          /* RoPE :351-365 */
+            int hd = i % hs;
+            float freq = 1.0f / powf(10000.0f, hd / (float)hs);
+            float val = pos * freq;
+            float fcr = cosf(val), fci = sinf(val);
+            int rotn = i < kv_dim ? 2 : 1;
+            for (int r = 0; r < rotn; r++) {
+                float* vec = r == 0 ? m->q : k;
+                float v0 = vec[i], v1 = vec[i + 1];
+                vec[i] = v0 * fcr - v1 * fci;
+                vec[i + 1] = v0 * fci + v1 * fcr;
+            }
+        }
+        for (int h = 0; h < p->n_heads; h++)                                         /* :369-391 */
+            mirror_attention(m->q + h * hs, m->kc + loff + (h / kv_mul) * hs, m->vc + loff + (h / kv_mul) * hs,
+                             (size_t)kv_dim, pos, hs, m->xb + h * hs);
+        mirror_act_quant(m->xb, NULL, dim, gs, m->aq, m->as, tmp);                   /* :394-396 */
+        mirror_gemv(m->xb2, &m->wo, l, dim, m->aq, m->as, dim, gs, kind, o_wo);
+        for (int i = 0; i < dim; i++) x[i] += m->xb2[i];
+        mirror_act_quant(x, m->rms_ffn + l * dim, dim, gs, m->aq, m->as, tmp);      /* :399-402 */
+        mirror_gemv(m->hb, &m->w1, l, hidden, m->aq, m->as, dim, gs, kind, o_ffn);
+        mirror_gemv(m->hb2, &m->w3, l, hidden, m->aq, m->as, dim, gs, kind, o_ffn);
+        for (int i = 0; i < hidden; i++) {                                           /* SwiGLU :405-410 */
+            float val = m->hb[i];
+            val = val * (1.0f / (1.0f + orc_expf(-val)));
+            m->hb[i] = val * m->hb2[i];
+        }
+        mirror_act_quant(m->hb, NULL, hidden, gs, m->aq, m->as, tmp);                /* :412-414 */
+        mirror_gemv(m->xb, &m->w2, l, dim, m->aq, m->as, hidden, gs, kind, o_w2);
+        for (int i = 0; i < dim; i++) x[i] += m->xb[i];
+    }
+    mirror_act_quant(x, m->rms_final, dim, gs, m->aq, m->as, tmp);                   /* :417-419 */
+    mirror_gemv(m->logits, &m->wcls, 0, p->vocab_size, m->aq, m->as, dim, gs, kind, o_cls);
+    free(tmp);
+    return m->logits;
+}

@@ -65,6 +65,13 @@ void orc_model_info(const OrcModel* m, OrcConfig* cfg, int* kind, int* gs);
 /* One token; returns the model-owned logits [vocab], overwritten by the
  * next call (runq.c:320 ownership). */
 float* orc_forward(OrcModel* m, int token, int pos);
+/* The same step evaluated in the B200 kernels' reduction order (fp32 sums
+ * associated as the device code does), for bit-exact comparison with the
+ * product.  Uses the model's own KV cache: do not mix with orc_forward on
+ * one model. */
+float* orc_forward_kernel_order(OrcModel* m, int token, int pos);
+/* exp as evaluated by the product (Cody-Waite + Taylor degree 7). */
+float orc_expf(float x);
 /* sample_argmax, runq.c:578-585: first index of the maximum. */
 int orc_argmax(const float* v, int n);
 

@@ -44,6 +44,10 @@ def orc() -> C.CDLL:
         L.orc_forward.restype = C.POINTER(C.c_float)
         L.orc_forward.argtypes = [_P, I, I]
         L.orc_argmax.argtypes = [_P, I]
+        L.orc_forward_kernel_order.restype = C.POINTER(C.c_float)
+        L.orc_forward_kernel_order.argtypes = [_P, I, I]
+        L.orc_expf.restype = C.c_float
+        L.orc_expf.argtypes = [C.c_float]
         _orc = L
     return _orc
 
@@ -130,6 +134,11 @@ class OracleModel:
 
     def forward(self, token: int, pos: int) -> np.ndarray:
         p = orc().orc_forward(self.h, token, pos)
+        return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def forward_kernel_order(self, token: int, pos: int) -> np.ndarray:
+        """The step in the product kernels' fp32 reduction order."""
+        p = orc().orc_forward_kernel_order(self.h, token, pos)
         return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
 
     def close(self):

@@ -96,3 +96,19 @@ def test_oracle_forward_tracks_runq(golden):
         assert int(np.argmax(lo)) == int(stream[pos])
         token = int(stream[pos])
     M.close()
+
+
+def test_kernel_order_oracle_tracks_runq(golden):
+    """The kernel-order oracle agrees with runq.c to a few ulp before any
+    int8 activation lands within an ulp of a rounding boundary (first three
+    golden positions), and within the documented flip bound after."""
+    g = golden("tiny_runq.npz")
+    import synth
+
+    M = O.OracleModel(synth.tiny_checkpoint(8, 32))
+    token, stream = 1, g["stream"]
+    for pos in range(3):
+        lo = M.forward_kernel_order(token, pos)
+        assert float(np.abs(lo - g[f"logits_{pos}"]).max() / np.abs(g[f"logits_{pos}"]).max()) < 1e-5
+        token = int(stream[pos])
+    M.close()
