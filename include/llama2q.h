@@ -136,6 +136,18 @@ int matmul(float* xout, const QuantizedTensor* x, const QuantizedTensor* w, int 
  * returns after the result is in xout. */
 int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int d);
 
+/* Allocation-free form of matmul_f32, for callers that cannot allocate device
+ * memory while they run (a host framework that owns all device memory and
+ * forbids allocation while serving, or a latency-bound loop that cannot
+ * afford a first-use cudaMalloc).  No counterpart in the reference.  Same
+ * result as matmul_f32; x and xout must be device memory.  Its scratch is a
+ * fixed 40 KB array in device memory held by every GPU that loads the
+ * library until exit: n is limited to 32768 (larger n returns LQ_EINVAL),
+ * every call on a device shares the array, and calls whose kernels overlap
+ * on the GPU race on it.  The first call on a device looks up the array's
+ * address; make that call before any stream capture. */
+int matmul_f32_noalloc(float* xout, const float* x, const QuantizedTensor* w, int n, int d);
+
 /* ---- model ------------------------------------------------------------- */
 
 /* Load a checkpoint: QLL8 version 1 (INT8, GS 32; tools/quantize_int8.py:11-37,

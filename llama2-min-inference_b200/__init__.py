@@ -80,7 +80,7 @@ class Config(C.Structure):
 EXPORTS = (
     "lq_last_error", "lq_select_device", "lq_set_stream", "lq_get_stream", "lq_sync",
     "lq_set_launch_flags", "lq_set_trace", "lq_graph_begin", "lq_graph_end", "lq_graph_launch", "lq_graph_destroy",
-    "lq_synth_tensor", "quantize", "matmul", "matmul_f32",
+    "lq_synth_tensor", "quantize", "matmul", "matmul_f32", "matmul_f32_noalloc",
     "build_transformer", "build_transformer_random", "forward", "forward_argmax",
     "free_transformer", "transformer_config",
     "lq_write_checkpoint_fp32", "lq_quantize_checkpoint", "lq_read_header", "lq_synth_value",
@@ -116,6 +116,7 @@ def lib() -> C.CDLL:
         "quantize": (I, [QT, P, I]),
         "matmul": (I, [P, QT, QT, I, I]),
         "matmul_f32": (I, [P, P, QT, I, I]),
+        "matmul_f32_noalloc": (I, [P, P, QT, I, I]),
         "build_transformer": (I, [C.POINTER(P), C.c_char_p, I]),
         "build_transformer_random": (I, [C.POINTER(P), CFG, I, I, U64, I]),
         "forward": (C.POINTER(F), [P, I, I]),
@@ -200,6 +201,11 @@ def matmul(xout_ptr: int, x: QuantizedTensor, w: QuantizedTensor, n: int, d: int
 def matmul_f32(xout_ptr: int, x_ptr: int, w: QuantizedTensor, n: int, d: int) -> None:
     """quantize_act + matmul_q8 in one call; host or device pointers."""
     check(lib().matmul_f32(C.c_void_p(xout_ptr), C.c_void_p(x_ptr), C.byref(w), n, d))
+
+
+def matmul_f32_noalloc(xout_ptr: int, x_ptr: int, w: QuantizedTensor, n: int, d: int) -> None:
+    """matmul_f32 without any device allocation (fixed library scratch, n <= 32768, device pointers)."""
+    check(lib().matmul_f32_noalloc(C.c_void_p(xout_ptr), C.c_void_p(x_ptr), C.byref(w), n, d))
 
 
 # ---- model -------------------------------------------------------------------
