@@ -247,6 +247,40 @@ def decode_bench(lq, torch, positions: int = 2048):
             "init_s": round(init_s, 2)}
 
 
+def batch_bench(lq, torch, batches=(1, 8, 16, 32, 64), ctx: int = 1024, steps: int = 8):
+    """Config 4: Llama-2-13B-shape batched decode, INT8 and INT4 GS64, B
+    independent sequences at context length ctx.  The KV cache positions
+    0..ctx-1 are zero-filled instead of decoded (attention reads every cached
+    position whatever its value, so the step's work is that of a real step at
+    that context); every timed step is a full forward_batch_argmax call."""
+    D, H, L, V = 5120, 13824, 40, 32000
+    cfg = lq.Config.make(D, H, L, 40, 40, V, 4096)
+    nmat = L * (4 * D * D + 3 * D * H) + V * D
+    out = {"config": "config4: llama-2-13b shape, gs64, fp32 KV at context %d" % ctx,
+           "timing": "host wall clock around %d forward_batch_argmax calls per batch size" % steps,
+           "kv_note": "cache positions below the context are zero-filled, not decoded", "runs": []}
+    for kind in (8, 4):
+        t = lq.Transformer.random(cfg, kind, 64, 11, ctx + steps + 8)
+        t.reserve_batch(max(batches))
+        wbytes = nmat * (1 if kind == 8 else 0.5) + nmat // 64 * 4
+        for B in batches:
+            tok = np.ones(B, np.int32)
+            for w in range(3):
+                tok = t.forward_batch_argmax(tok, np.full(B, ctx - 3 + w, np.int32))
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for s_ in range(steps):
+                tok = t.forward_batch_argmax(tok, np.full(B, ctx + s_, np.int32))
+            dt = (time.perf_counter() - t0) / steps
+            kv = B * 2 * L * D * 4 * (ctx + steps / 2)
+            gbs = (wbytes + kv) / dt / 1e9
+            out["runs"].append({"weight_kind": "int%d" % kind, "batch": B, "tok_s": round(B / dt, 1),
+                                "ms_per_step": round(1e3 * dt, 3), "weight_bytes": int(wbytes),
+                                "kv_bytes_per_step": int(kv), "hbm_gbs_effective": round(gbs, 1)})
+        t.close()
+    return out
+
+
 def run_gpu(args):
     import torch
 
@@ -351,6 +385,11 @@ def run_gpu(args):
             extra["decode"] = decode_bench(lq, torch, args.decode_positions)
         except Exception as e:  # reported, never hides the GEMV line
             extra["decode"] = {"error": str(e)[:300]}
+    if rank == 0 and world == 1 and not args.no_batch:
+        try:
+            extra["batched"] = batch_bench(lq, torch)
+        except Exception as e:
+            extra["batched"] = {"error": str(e)[:300]}
 
     if rank == 0:
         peak, peak_kind = peaks()
@@ -393,6 +432,7 @@ def main():
     ap.add_argument("--decode-positions", type=int, default=2048)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-batch", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -177,6 +177,27 @@ float* forward(Transformer* t, int token, int pos);
  * to *next_token and copies 4 bytes instead of the logits. */
 int forward_argmax(Transformer* t, int token, int pos, int* next_token);
 
+/* ---- batched decode (B independent sequences, one token each per step) ---
+ * The reference decodes one sequence; its batched kernel is the prompt-time
+ * matmul_q8_kernel of v2-cuda/run.cu:131-162 (T rows against one weight
+ * stream).  Here B sequences each hold their own KV cache and position and
+ * advance together: every weight byte is streamed once per step for all B
+ * rows.  Sequence b uses cache slot b; row b of the step is independent of
+ * every other row (its logits are bitwise those of a batch-1 forward with the
+ * same history). */
+
+/* Size the model for up to max_batch sequences (default 1).  Releases and
+ * re-creates the activations and KV caches: every sequence restarts. */
+int transformer_reserve_batch(Transformer* t, int max_batch);
+
+/* One decode step for sequences 0..batch-1: tokens[b] at positions pos[b].
+ * Returns host logits [batch][vocab] owned by t and valid until the next call,
+ * or NULL on error (lq_last_error()). */
+float* forward_batch(Transformer* t, const int* tokens, const int* pos, int batch);
+
+/* As forward_batch, writing only the greedy next token of every sequence. */
+int forward_batch_argmax(Transformer* t, const int* tokens, const int* pos, int batch, int* next_tokens);
+
 /* Release a model (free_transformer, runq.c:285-289). */
 void free_transformer(Transformer* t);
 

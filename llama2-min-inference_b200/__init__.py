@@ -82,6 +82,7 @@ EXPORTS = (
     "lq_set_launch_flags", "lq_set_trace", "lq_graph_begin", "lq_graph_end", "lq_graph_launch", "lq_graph_destroy",
     "lq_synth_tensor", "quantize", "matmul", "matmul_f32", "matmul_f32_noalloc",
     "build_transformer", "build_transformer_random", "forward", "forward_argmax",
+    "transformer_reserve_batch", "forward_batch", "forward_batch_argmax",
     "free_transformer", "transformer_config",
     "lq_write_checkpoint_fp32", "lq_quantize_checkpoint", "lq_read_header", "lq_synth_value",
 )
@@ -121,6 +122,9 @@ def lib() -> C.CDLL:
         "build_transformer_random": (I, [C.POINTER(P), CFG, I, I, U64, I]),
         "forward": (C.POINTER(F), [P, I, I]),
         "forward_argmax": (I, [P, I, I, C.POINTER(I)]),
+        "transformer_reserve_batch": (I, [P, I]),
+        "forward_batch": (C.POINTER(F), [P, P, P, I]),
+        "forward_batch_argmax": (I, [P, P, P, I, P]),
         "free_transformer": (None, [P]),
         "transformer_config": (I, [P, CFG, C.POINTER(I), C.POINTER(I)]),
         "lq_write_checkpoint_fp32": (I, [C.c_char_p, CFG, U64, F, I]),
@@ -244,6 +248,39 @@ class Transformer:
         nxt = C.c_int()
         check(lib().forward_argmax(self._h, token, pos, C.byref(nxt)))
         return nxt.value
+
+    def reserve_batch(self, max_batch: int) -> None:
+        """Size for up to max_batch sequences (restarts every sequence)."""
+        check(lib().transformer_reserve_batch(self._h, max_batch))
+        self.max_batch = max_batch
+
+    @staticmethod
+    def _rows(tokens, pos):
+        import numpy as np
+
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = np.ascontiguousarray(pos, dtype=np.int32)
+        if t.shape != p.shape or t.ndim != 1:
+            raise ValueError("tokens and pos must be 1-D and of equal length")
+        return t, p
+
+    def forward_batch(self, tokens, pos):
+        """Logits [B, vocab] (a view of host memory valid until the next call)."""
+        import numpy as np
+
+        t, p = self._rows(tokens, pos)
+        r = lib().forward_batch(self._h, t.ctypes.data, p.ctypes.data, t.size)
+        if not r:
+            raise LlamaQError(-1, last_error())
+        return np.ctypeslib.as_array(r, shape=(t.size, self.config.vocab_size))
+
+    def forward_batch_argmax(self, tokens, pos):
+        import numpy as np
+
+        t, p = self._rows(tokens, pos)
+        out = np.empty(t.size, np.int32)
+        check(lib().forward_batch_argmax(self._h, t.ctypes.data, p.ctypes.data, t.size, out.ctypes.data))
+        return out
 
     def close(self) -> None:
         if self._h:

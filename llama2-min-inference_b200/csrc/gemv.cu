@@ -371,6 +371,7 @@ __device__ __forceinline__ void rope_pair(const float2* rope, float& v0, float& 
 // EPI_SWIGLU, v0/v1 are the w1 row values and u0/u1 the w3 row values.
 __device__ void finish_rows(const GemvArgs& a, const GemvSeg& g, int b, int r, float v0, float v1, float u0,
                             float u1, bool has2) {
+    if (b >= a.nvalid) return;  // padding row of a partial batch chunk
     const int pos = (g.epi == EPI_ROPE_Q || g.epi == EPI_ROPE_KCACHE || g.epi == EPI_VCACHE) ? a.meta[2 * b + 1] : 0;
     switch (g.epi) {
         case EPI_STORE: {
@@ -1132,6 +1133,7 @@ static int g_ctas_per_sm = 0;
 
 cudaError_t gemv_launch(GemvArgs a, int kind, cudaStream_t st, bool pdl, int num_sms) {
     if (!gemv_args_ok(a, kind)) return cudaErrorInvalidValue;
+    if (a.nvalid <= 0 || a.nvalid > a.nb) a.nvalid = a.nb;
     if (!g_ctas_per_sm) {
         const char* e = getenv("LQ_GEMV_CTAS_PER_SM");
         g_ctas_per_sm = e ? atoi(e) : 4;

@@ -44,6 +44,7 @@ struct GemvArgs {
     int cols;        // n (input length)
     int gs;          // group size: 32, 64, 128 or 256
     int nb;          // activation rows (batch); template NB must equal it
+    int nvalid;      // rows b < nvalid are stored; rows nvalid..nb-1 are padding (0 = all)
     // input
     int in_mode;
     const int8_t* xq;  // IN_QUANT [nb, cols]

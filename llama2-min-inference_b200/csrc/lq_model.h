@@ -15,7 +15,7 @@ struct QW {
 
 int forward_launch(Transformer* t, int batch);
 int run_step(Transformer* t, const int* tokens, const int* pos, int batch, bool want_logits, bool want_next);
-int kernels_per_step(const Transformer* t);
+int kernels_per_step(const Transformer* t, int batch);
 
 }  // namespace lq
 

@@ -103,9 +103,12 @@ int alloc_state(Transformer* t) {
     rc = rc ? rc : dalloc(&t->h3, (size_t)B * c.hidden_dim);
     rc = rc ? rc : dalloc(&t->logits, (size_t)B * c.vocab_size);
     const int maxn = c.hidden_dim > c.dim ? c.hidden_dim : c.dim;
-    rc = rc ? rc : dalloc(&t->xq, (size_t)B * maxn);
-    rc = rc ? rc : dalloc(&t->xqs, (size_t)B * (maxn / t->gs));
-    rc = rc ? rc : dalloc(&t->xqsum, (size_t)B * (maxn / t->gs));
+    // the quantized activation has padding rows up to a multiple of 8: a
+    // GEMV launch reads 1, 2, 4 or 8 rows and stores only the valid ones
+    const int BP = (B + 7) / 8 * 8;
+    rc = rc ? rc : dalloc(&t->xq, (size_t)BP * maxn);
+    rc = rc ? rc : dalloc(&t->xqs, (size_t)BP * (maxn / t->gs));
+    rc = rc ? rc : dalloc(&t->xqsum, (size_t)BP * (maxn / t->gs));
     rc = rc ? rc : dalloc(&t->kc, kv);
     rc = rc ? rc : dalloc(&t->vc, kv);
     rc = rc ? rc : dalloc(&t->part, (size_t)B * c.n_heads * t->max_splits * (t->head_size + 2));
@@ -129,6 +132,9 @@ int alloc_state(Transformer* t) {
         if (e0 != cudaSuccess) return cuda_fail(e0, "rope table");
     }
     cudaError_t e = cudaMemset(t->counters, 0, (size_t)B * c.n_kv_heads * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(t->xq, 0, (size_t)BP * maxn);
+    if (e == cudaSuccess) e = cudaMemset(t->xqs, 0, (size_t)BP * (maxn / t->gs) * sizeof(float));
+    if (e == cudaSuccess) e = cudaMemset(t->xqsum, 0, (size_t)BP * (maxn / t->gs) * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(t->err, 0, sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(t->meta, 0, 2 * B * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(t->kc, 0, kv * sizeof(float));
@@ -137,9 +143,67 @@ int alloc_state(Transformer* t) {
     if (e == cudaSuccess) e = cudaMallocHost(&t->h_meta, 2 * B * sizeof(int) + 64);
     if (e == cudaSuccess) e = cudaMallocHost(&t->h_next, B * sizeof(int) + 64);
     if (e == cudaSuccess) e = cudaMallocHost(&t->h_err, 64);
-    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&t->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess && !t->stream) e = cudaStreamCreateWithFlags(&t->stream, cudaStreamNonBlocking);
     if (e != cudaSuccess) return cuda_fail(e, "state allocation");
     return LQ_OK;
+}
+
+// release the per-sequence state (activations, caches, host mirrors, graph)
+void free_state(Transformer* t) {
+    if (t->stream) cudaStreamSynchronize(t->stream);
+    if (t->exec) cudaGraphExecDestroy(t->exec);
+    if (t->graph) cudaGraphDestroy(t->graph);
+    t->exec = nullptr;
+    t->graph = nullptr;
+    t->graph_batch = 0;
+    void* bufs[] = {t->x, t->q, t->att, t->h1, t->h3, t->xq, t->xqs, t->xqsum, t->logits, t->kc, t->vc,
+                    t->part, t->counters, t->meta, t->next, t->err, t->rope};
+    for (void* b : bufs) cudaFree(b);
+    t->x = t->q = t->att = t->h1 = t->h3 = t->logits = t->kc = t->vc = t->part = nullptr;
+    t->xq = nullptr;
+    t->xqs = nullptr;
+    t->xqsum = t->counters = t->meta = t->next = t->err = nullptr;
+    t->rope = nullptr;
+    cudaFreeHost(t->h_logits);
+    cudaFreeHost(t->h_meta);
+    cudaFreeHost(t->h_next);
+    cudaFreeHost(t->h_err);
+    t->h_logits = nullptr;
+    t->h_meta = t->h_next = t->h_err = nullptr;
+}
+
+// rows per GEMV launch: the largest kernel row count (8, 4, 2, 1) whose int8
+// activation rows fit the shared-memory budget of the bulk-copy kernel
+int gemv_chunk(int cols) {
+    for (int nb = 8; nb > 1; nb /= 2)
+        if ((int64_t)nb * cols <= 112 * 1024) return nb;
+    return 1;
+}
+
+// One GEMV over `batch` activation rows: launches of up to gemv_chunk rows,
+// the last one rounded up to a kernel row count with the extra rows unstored.
+cudaError_t gemv_rows(const GemvArgs& a, int kind, int batch, cudaStream_t st, int num_sms) {
+    const int chunk = gemv_chunk(a.cols);
+    const int ng = a.cols / a.gs;
+    for (int b0 = 0; b0 < batch; b0 += chunk) {
+        const int left = batch - b0;
+        int nb = 1;
+        while (nb < left && nb < chunk) nb *= 2;
+        GemvArgs c = a;
+        c.nb = nb;
+        c.nvalid = left < nb ? left : nb;
+        c.xq = a.xq + (size_t)b0 * a.cols;
+        c.xs = a.xs + (size_t)b0 * ng;
+        c.xsum_in = a.xsum_in ? a.xsum_in + (size_t)b0 * ng : nullptr;
+        c.meta = a.meta + 2 * b0;
+        for (int i = 0; i < c.nseg; ++i)
+            if (c.seg[i].y) c.seg[i].y += (size_t)b0 * a.y_stride;
+        if (c.kcache) c.kcache += (size_t)b0 * a.kv_seq_stride;
+        if (c.vcache) c.vcache += (size_t)b0 * a.kv_seq_stride;
+        cudaError_t e = gemv_launch(c, kind, st, true, num_sms);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
 }
 
 Transformer* new_transformer(const Config* c, int kind, int gs, int max_seq, int max_batch) {
@@ -218,7 +282,7 @@ int forward_launch(Transformer* t, int batch) {
         qin(a);
         a.kcache = t->kc + l * kv_layer;
         a.vcache = t->vc + l * kv_layer;
-        if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
+        if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
         // 2. attention
         AttnArgs at{};
         at.q = t->q;
@@ -243,7 +307,7 @@ int forward_launch(Transformer* t, int batch) {
         a.seg[0] = {t->wo.q + (size_t)l * D * rbD, t->wo.s + (size_t)l * D * ngD, t->x, D, EPI_ADD};
         a.nseg = 1;
         qin(a);
-        if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "wo gemv");
+        if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "wo gemv");
         // 4. w1 | w3 paired, SwiGLU in the epilogue: h1 = silu(x.w1) * (x.w3)
         if ((e = quant(IN_RMSNORM, t->x, D, t->rms_ffn + (size_t)l * D)) != cudaSuccess)
             return cuda_fail(e, "ffn rmsnorm");
@@ -254,14 +318,14 @@ int forward_launch(Transformer* t, int batch) {
         a.paired = 1;
         a.y_stride = H;
         qin(a);
-        if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w1/w3 gemv");
+        if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w1/w3 gemv");
         // 5. w2 + residual
         if ((e = quant(IN_F32, t->h1, H, nullptr)) != cudaSuccess) return cuda_fail(e, "ffn quantize");
         base(a, H);
         a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->x, D, EPI_ADD};
         a.nseg = 1;
         qin(a);
-        if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
+        if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
     }
     GemvArgs a;
     if ((e = quant(IN_RMSNORM, t->x, D, t->rms_final)) != cudaSuccess) return cuda_fail(e, "final rmsnorm");
@@ -270,13 +334,18 @@ int forward_launch(Transformer* t, int batch) {
     a.nseg = 1;
     a.y_stride = c.vocab_size;
     qin(a);
-    if ((e = gemv_launch(a, kind, st, true, t->num_sms)) != cudaSuccess) return cuda_fail(e, "classifier gemv");
+    if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "classifier gemv");
     if ((e = argmax_launch(t->logits, c.vocab_size, batch, c.vocab_size, t->next, st, true)) != cudaSuccess)
         return cuda_fail(e, "argmax");
     return LQ_OK;
 }
 
-int kernels_per_step(const Transformer* t) { return 9 * t->c.n_layers + 3; }
+int kernels_per_step(const Transformer* t, int batch) {
+    const int cd = gemv_chunk(t->c.dim), ch = gemv_chunk(t->c.hidden_dim);
+    const int gd = (batch + cd - 1) / cd, gh = (batch + ch - 1) / ch;
+    // per layer: 4 quantizers, attention, GEMVs qkv / wo / w1|w3 (dim inputs) and w2 (hidden inputs)
+    return t->c.n_layers * (5 + 3 * gd + gh) + 2 + gd;
+}
 
 static int ensure_graph(Transformer* t, int batch) {
     if (t->exec && t->graph_batch == batch) return LQ_OK;
@@ -307,7 +376,9 @@ static int ensure_graph(Transformer* t, int batch) {
 
 // One step for `batch` sequences: H2D tokens/positions, graph, optional D2H.
 int run_step(Transformer* t, const int* tokens, const int* pos, int batch, bool want_logits, bool want_next) {
-    if (batch < 1 || batch > t->max_batch) return lq_fail(LQ_EINVAL, "batch %d out of range", batch);
+    if (!t->x) return lq_fail(LQ_EINVAL, "model has no decode state (a failed transformer_reserve_batch)");
+    if (batch < 1 || batch > t->max_batch)
+        return lq_fail(LQ_EINVAL, "batch %d out of range [1, %d]", batch, t->max_batch);
     for (int b = 0; b < batch; ++b) {
         if (tokens[b] < 0 || tokens[b] >= t->c.vocab_size)
             return lq_fail(LQ_EINVAL, "token %d out of range [0, %d)", tokens[b], t->c.vocab_size);
@@ -481,23 +552,42 @@ int forward_argmax(Transformer* t, int token, int pos, int* next_token) {
 
 void free_transformer(Transformer* t) {
     if (!t) return;
-    if (t->stream) cudaStreamSynchronize(t->stream);
-    if (t->exec) cudaGraphExecDestroy(t->exec);
-    if (t->graph) cudaGraphDestroy(t->graph);
+    free_state(t);
     QW* ws[] = {&t->wq, &t->wk, &t->wv, &t->wo, &t->w1, &t->w2, &t->w3, &t->wcls};
     for (QW* w : ws) {
         cudaFree(w->q);
         cudaFree(w->s);
     }
-    void* bufs[] = {t->emb, t->rms_att, t->rms_ffn, t->rms_final, t->x, t->q, t->att, t->h1, t->h3, t->xq, t->xqs, t->xqsum,
-                    t->logits, t->kc, t->vc, t->part, t->counters, t->meta, t->next, t->err, t->rope};
+    void* bufs[] = {t->emb, t->rms_att, t->rms_ffn, t->rms_final};
     for (void* b : bufs) cudaFree(b);
-    cudaFreeHost(t->h_logits);
-    cudaFreeHost(t->h_meta);
-    cudaFreeHost(t->h_next);
-    cudaFreeHost(t->h_err);
     if (t->stream) cudaStreamDestroy(t->stream);
     delete t;
+}
+
+int transformer_reserve_batch(Transformer* t, int max_batch) {
+    if (!t) return lq_fail(LQ_EINVAL, "transformer_reserve_batch: null transformer");
+    if (max_batch < 1 || max_batch > 1024) return lq_fail(LQ_EINVAL, "max_batch %d out of range [1, 1024]", max_batch);
+    free_state(t);
+    t->max_batch = max_batch;
+    cudaGetLastError();
+    return alloc_state(t);
+}
+
+float* forward_batch(Transformer* t, const int* tokens, const int* pos, int batch) {
+    if (!t || !tokens || !pos) {
+        lq_fail(LQ_EINVAL, "forward_batch: null argument");
+        return nullptr;
+    }
+    if (run_step(t, tokens, pos, batch, true, false) != LQ_OK) return nullptr;
+    return t->h_logits;
+}
+
+int forward_batch_argmax(Transformer* t, const int* tokens, const int* pos, int batch, int* next_tokens) {
+    if (!t || !tokens || !pos || !next_tokens) return lq_fail(LQ_EINVAL, "forward_batch_argmax: null argument");
+    int rc = run_step(t, tokens, pos, batch, false, true);
+    if (rc) return rc;
+    for (int b = 0; b < batch; ++b) next_tokens[b] = t->h_next[b];
+    return LQ_OK;
 }
 
 int transformer_config(const Transformer* t, Config* cfg, int* kind, int* group_size) {
