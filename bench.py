@@ -249,21 +249,35 @@ def decode_bench(lq, torch, positions: int = 2048):
 
 def batch_bench(lq, torch, batches=(1, 8, 16, 32, 64), ctx: int = 1024, steps: int = 8):
     """Config 4: Llama-2-13B-shape batched decode, INT8 and INT4 GS64, B
-    independent sequences at context length ctx.  The KV cache positions
-    0..ctx-1 are zero-filled instead of decoded (attention reads every cached
-    position whatever its value, so the step's work is that of a real step at
-    that context); every timed step is a full forward_batch_argmax call."""
+    independent sequences at context length ctx.  From 16 sequences on the
+    products run on the tensor cores (tcgen05 kind::i8); the dp4a GEMV is
+    also timed at 16 and 64 sequences for the crossover.  The KV cache
+    positions 0..ctx-1 are zero-filled instead of decoded (attention reads
+    every cached position whatever its value, so the step's work is that of
+    a real step at that context); every timed step is a full
+    forward_batch_argmax call."""
     D, H, L, V = 5120, 13824, 40, 32000
     cfg = lq.Config.make(D, H, L, 40, 40, V, 4096)
     nmat = L * (4 * D * D + 3 * D * H) + V * D
     out = {"config": "config4: llama-2-13b shape, gs64, fp32 KV at context %d" % ctx,
            "timing": "host wall clock around %d forward_batch_argmax calls per batch size" % steps,
            "kv_note": "cache positions below the context are zero-filled, not decoded", "runs": []}
-    for kind in (8, 4):
-        t = lq.Transformer.random(cfg, kind, 64, 11, ctx + steps + 8)
-        t.reserve_batch(max(batches))
+    plans = [(8, None, batches), (4, None, batches), (8, "1000", (16, 64)), (4, "1000", (16, 64))]
+    for kind, mma_env, bs in plans:
+        old = os.environ.get("LQ_MMA_MIN_ROWS")
+        if mma_env is not None:
+            os.environ["LQ_MMA_MIN_ROWS"] = mma_env
+        try:
+            t = lq.Transformer.random(cfg, kind, 64, 11, ctx + steps + 8)
+        finally:
+            if mma_env is not None:
+                if old is None:
+                    os.environ.pop("LQ_MMA_MIN_ROWS", None)
+                else:
+                    os.environ["LQ_MMA_MIN_ROWS"] = old
+        t.reserve_batch(max(bs))
         wbytes = nmat * (1 if kind == 8 else 0.5) + nmat // 64 * 4
-        for B in batches:
+        for B in bs:
             tok = np.ones(B, np.int32)
             for w in range(3):
                 tok = t.forward_batch_argmax(tok, np.full(B, ctx - 3 + w, np.int32))
@@ -274,7 +288,8 @@ def batch_bench(lq, torch, batches=(1, 8, 16, 32, 64), ctx: int = 1024, steps: i
             dt = (time.perf_counter() - t0) / steps
             kv = B * 2 * L * D * 4 * (ctx + steps / 2)
             gbs = (wbytes + kv) / dt / 1e9
-            out["runs"].append({"weight_kind": "int%d" % kind, "batch": B, "tok_s": round(B / dt, 1),
+            path = "tcgen05 kind::i8" if (B >= 16 and mma_env is None) else "dp4a GEMV"
+            out["runs"].append({"weight_kind": "int%d" % kind, "batch": B, "path": path, "tok_s": round(B / dt, 1),
                                 "ms_per_step": round(1e3 * dt, 3), "weight_bytes": int(wbytes),
                                 "kv_bytes_per_step": int(kv), "hbm_gbs_effective": round(gbs, 1)})
         t.close()

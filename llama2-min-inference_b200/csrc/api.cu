@@ -2,6 +2,7 @@
 // (quantize / matmul / matmul_f32).
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -257,6 +258,42 @@ int quantize(QuantizedTensor* out, const float* x, int n) {
     return LQ_OK;
 }
 
+constexpr int kQgMaxTiles = 4096;
+
+static int mma_min_rows() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("LQ_MMA_MIN_ROWS");
+        v = e ? atoi(e) : 16;
+        if (v < 1) v = 1 << 30;  // 0 or negative: never
+    }
+    return v;
+}
+
+// workspace of the tensor-core GEMM (allocated outside graph capture)
+static int ensure_qgemm(DevCtx* c, int ng) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    const bool capturing = cudaStreamIsCapturing(g_stream, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone;
+    const size_t xst = (size_t)ng * 64;
+    if (c->qg_part && c->qg_xst_floats >= xst) return LQ_OK;
+    if (capturing)
+        return lq_fail(LQ_EINVAL, "matmul: tensor-core workspace needed inside a graph capture: make one call first");
+    cudaError_t e = cudaSuccess;
+    if (!c->qg_part) {
+        e = cudaMalloc(&c->qg_part, qgemm_part_floats(c->num_sms) * sizeof(float));
+        if (e == cudaSuccess) e = cudaMalloc(&c->qg_cnt, kQgMaxTiles * sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(c->qg_cnt, 0, kQgMaxTiles * sizeof(int));
+    }
+    if (e == cudaSuccess && c->qg_xst_floats < xst) {
+        if (c->qg_xst) cudaFree(c->qg_xst);
+        c->qg_xst = nullptr;
+        c->qg_xst_floats = 0;
+        e = cudaMalloc(&c->qg_xst, xst * sizeof(float));
+        if (e == cudaSuccess) c->qg_xst_floats = xst;
+    }
+    return e == cudaSuccess ? LQ_OK : cuda_fail(e, "tensor-core GEMM workspace");
+}
+
 static int check_weight(const QuantizedTensor* w, int n, int d, const char* fn) {
     if (!w || !w->q || !w->s) return lq_fail(LQ_EINVAL, "%s: weight tensor not set", fn);
     if (w->kind != LQ_KIND_INT8 && w->kind != LQ_KIND_INT4)
@@ -283,6 +320,38 @@ int matmul(float* xout, const QuantizedTensor* x, const QuantizedTensor* w, int 
     if (!c) return lq_fail(LQ_ECUDA, "no CUDA device context (no device, or first use inside a graph capture)");
     const int ng = n / w->group_size;
     int64_t done = 0;
+    if (x->rows >= mma_min_rows()) {
+        // tensor cores: up to 64 activation rows per launch
+        GemvArgs a = {};
+        a.seg[0] = {static_cast<const uint8_t*>(w->q), w->s, xout, d, EPI_STORE};
+        a.nseg = 1;
+        a.cols = n;
+        a.gs = w->group_size;
+        a.in_mode = IN_QUANT;
+        a.xq = static_cast<const int8_t*>(x->q);
+        a.y_stride = d;
+        a.err = c->err;
+        a.nb = a.nvalid = 16;
+        if (qgemm_ok(a, w->kind, 16) && d / 128 <= kQgMaxTiles) {
+            rc = ensure_qgemm(c, ng);
+            if (rc) return rc;
+            const float mul = w->kind == LQ_KIND_INT4 ? 0.0625f : 1.0f;
+            while (done < x->rows) {
+                const int rows = (int)(x->rows - done < 64 ? x->rows - done : 64);
+                const int npad = qgemm_npad(rows);
+                cudaError_t e = qgemm_scales_launch(x->s + done * ng, rows, ng, npad, mul, c->qg_xst, g_stream);
+                a.seg[0].y = xout + done * d;
+                a.xq = static_cast<const int8_t*>(x->q) + done * n;
+                a.nb = a.nvalid = rows;
+                if (e == cudaSuccess)
+                    e = qgemm_launch(a, w->kind, c->qg_xst, npad, c->qg_part, c->qg_cnt, g_stream,
+                                     g_launch_flags & LQ_LAUNCH_PDL, c->num_sms);
+                if (e != cudaSuccess) return cuda_fail(e, "matmul (tensor cores) launch");
+                done += rows;
+            }
+            return LQ_OK;
+        }
+    }
     while (done < x->rows) {
         const int64_t left = x->rows - done;
         const int nb = left >= 8 ? 8 : left >= 4 ? 4 : left >= 2 ? 2 : 1;

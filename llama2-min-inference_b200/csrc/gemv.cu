@@ -39,6 +39,7 @@
 #include <cstdlib>
 
 #include "lq_device.cuh"
+#include "lq_epilogue.cuh"
 #include "lq_kernels.h"
 #include "lq_math.h"
 
@@ -353,59 +354,7 @@ __device__ __forceinline__ void block_dot(const uint8_t* const* rows, const floa
     }
 }
 
-// ---------------------------------------------------------------------------
-// epilogue
-
-// RoPE, v1-int8-vnni/runq.c:351-365.  cos/sin of pos * freq come from a
-// table the host fills with the reference's own formula (1/powf(10000,
-// hd/hs), cosf, sinf), so the rotation needs no device transcendentals and
-// matches the CPU bit for bit.
-__device__ __forceinline__ void rope_pair(const float2* rope, float& v0, float& v1, int r, int head_size, int pos) {
-    const float2 cs = rope[(size_t)pos * (head_size >> 1) + ((r % head_size) >> 1)];
-    const float a0 = v0, a1 = v1;
-    v0 = a0 * cs.x - a1 * cs.y;
-    v1 = a0 * cs.y + a1 * cs.x;
-}
-
-// Finish rows r and r+1 (when has2) of segment g for batch row b.  For
-// EPI_SWIGLU, v0/v1 are the w1 row values and u0/u1 the w3 row values.
-__device__ void finish_rows(const GemvArgs& a, const GemvSeg& g, int b, int r, float v0, float v1, float u0,
-                            float u1, bool has2) {
-    if (b >= a.nvalid) return;  // padding row of a partial batch chunk
-    const int pos = (g.epi == EPI_ROPE_Q || g.epi == EPI_ROPE_KCACHE || g.epi == EPI_VCACHE) ? a.meta[2 * b + 1] : 0;
-    switch (g.epi) {
-        case EPI_STORE: {
-            float* y = g.y + (size_t)b * a.y_stride;
-            y[r] = v0;
-            if (has2) y[r + 1] = v1;
-        } break;
-        case EPI_ADD: {
-            float* y = g.y + (size_t)b * a.y_stride;
-            y[r] += v0;
-            if (has2) y[r + 1] += v1;
-        } break;
-        case EPI_SWIGLU: {
-            float* y = g.y + (size_t)b * a.y_stride;
-            y[r] = lq_swiglu(v0, u0);
-            if (has2) y[r + 1] = lq_swiglu(v1, u1);
-        } break;
-        case EPI_ROPE_Q: {
-            rope_pair(a.rope, v0, v1, r, a.head_size, pos);
-            float* y = g.y + (size_t)b * a.y_stride;
-            y[r] = v0;
-            y[r + 1] = v1;
-        } break;
-        case EPI_ROPE_KCACHE:
-        case EPI_VCACHE: {
-            if (g.epi == EPI_ROPE_KCACHE) rope_pair(a.rope, v0, v1, r, a.head_size, pos);
-            float* c = (g.epi == EPI_ROPE_KCACHE ? a.kcache : a.vcache) + (size_t)b * a.kv_seq_stride;
-            const int hs = a.head_size;
-            const size_t o = ((size_t)(r / hs) * a.max_seq + pos) * hs + (r % hs);
-            c[o] = v0;
-            if (has2) c[o + 1] = v1;  // r even, hs even: r+1 is in the same head
-        } break;
-    }
-}
+// epilogue (rope_pair, finish_rows): lq_epilogue.cuh
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -972,6 +921,7 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_cons
         const int g = task / lpg;
         a.xs[(size_t)b * ng + g] = sc;
         a.xsum[(size_t)b * ng + g] = qs;
+        if (a.xs_t) a.xs_t[(size_t)g * a.npad + b] = sc * a.xs_t_mul;
     }
 }
 

@@ -14,6 +14,11 @@ struct DevCtx {
     int* err = nullptr;         // device error word for stand-alone operator calls
     void* scratch = nullptr;    // staging for host-pointer calls
     size_t scratch_bytes = 0;
+    // tensor-core GEMM (matmul with >= 16 activation rows)
+    float* qg_part = nullptr;   // stream-K partials
+    int* qg_cnt = nullptr;      // per-tile arrival counters (left zero by every launch)
+    float* qg_xst = nullptr;    // transposed activation scales [ng][64]
+    size_t qg_xst_floats = 0;
 };
 
 DevCtx* ctx();  // context of the current device (created on first use)

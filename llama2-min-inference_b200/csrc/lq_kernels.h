@@ -75,6 +75,22 @@ struct GemvArgs {
     int paired;      // segments carry a second tensor (EPI_SWIGLU)
 };
 
+// Tensor-core GEMM (tcgen05.mma kind::i8) for 1..64 activation rows:
+// segments and epilogues as for the GEMV; a.xq = int8 activation of
+// a.nvalid rows of a.cols bytes (the kernel pads to qgemm_npad(rows) with
+// zero rows); xs_t = activation scales transposed [cols/gs][xs_ld] (1/16 of
+// them for INT4 weights), xs_ld >= qgemm_npad(rows); part =
+// qgemm_part_floats(num_sms) floats of scratch; cnt = per-tile arrival
+// counters, zero-initialised, left zero.
+bool qgemm_ok(const GemvArgs& a, int kind, int rows);
+int qgemm_npad(int rows);
+size_t qgemm_part_floats(int num_sms);
+int qgemm_max_tiles(const GemvArgs& a);
+cudaError_t qgemm_launch(const GemvArgs& a, int kind, const float* xs_t, int xs_ld, float* part, int* cnt,
+                         cudaStream_t st, bool pdl, int num_sms);
+// xs [rows][ng] -> xs_t [ng][ld] times mul (columns >= rows zero)
+cudaError_t qgemm_scales_launch(const float* xs, int rows, int ng, int ld, float mul, float* xs_t, cudaStream_t st);
+
 // Activation quantization kernel (quantize_act, v1-int8-vnni/runq.c:117-139,
 // optionally after rmsnorm, runq.c:294-305): writes int8 xq [nb, n] in
 // natural order, fp32 scales xs and int32 group sums xsum [nb, n/gs].
@@ -89,6 +105,11 @@ struct ActQuantArgs {
     int8_t* xq;
     float* xs;
     int* xsum;
+    // optional (tensor-core GEMM input): scales transposed to [n/gs][npad],
+    // multiplied by xs_t_mul (1, or 1/16 for int4 weights held as 16*q)
+    float* xs_t;
+    int npad;
+    float xs_t_mul;
 };
 cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl);
 

@@ -41,6 +41,12 @@ struct Transformer {
     int* next = nullptr;                 // [B] argmax
     int* err = nullptr;                  // device error word
     float2* rope = nullptr;              // [max_seq][head_size/2] cos/sin table
+    // tensor-core GEMM path (steps of mma_min or more sequences)
+    int mma_min = 16;
+    int xs_ld = 0;                       // leading dimension of xs_t (max_batch rounded up to 64)
+    float* xs_t = nullptr;               // activation scales transposed [max groups][xs_ld]
+    float* qg_part = nullptr;            // stream-K partials
+    int* qg_cnt = nullptr;               // per-tile arrival counters
     // pinned host mirrors
     float* h_logits = nullptr;
     int *h_meta = nullptr, *h_next = nullptr, *h_err = nullptr;

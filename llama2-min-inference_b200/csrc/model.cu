@@ -38,6 +38,8 @@ namespace {
 
 int64_t rbytes(int64_t cols, int kind) { return kind == LQ_KIND_INT8 ? cols : cols / 2; }
 
+constexpr int kQgTiles = 8192;  // arrival counters: tiles of the largest launch (vocab / 128)
+
 int alloc_q(QW& w, int64_t rows, int64_t cols, int gs, int kind) {
     w.rows = rows;
     w.cols = cols;
@@ -117,6 +119,10 @@ int alloc_state(Transformer* t) {
     rc = rc ? rc : dalloc(&t->next, (size_t)B);
     rc = rc ? rc : dalloc(&t->err, 1);
     rc = rc ? rc : dalloc(&t->rope, (size_t)t->max_seq * (t->head_size / 2));
+    t->xs_ld = (B + 63) / 64 * 64;
+    rc = rc ? rc : dalloc(&t->xs_t, (size_t)t->xs_ld * (maxn / t->gs));
+    rc = rc ? rc : dalloc(&t->qg_part, qgemm_part_floats(t->num_sms));
+    rc = rc ? rc : dalloc(&t->qg_cnt, (size_t)kQgTiles);
     if (rc) return rc;
     {
         // RoPE table with the reference's arithmetic (runq.c:352-356)
@@ -132,6 +138,8 @@ int alloc_state(Transformer* t) {
         if (e0 != cudaSuccess) return cuda_fail(e0, "rope table");
     }
     cudaError_t e = cudaMemset(t->counters, 0, (size_t)B * c.n_kv_heads * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(t->qg_cnt, 0, (size_t)kQgTiles * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(t->xs_t, 0, (size_t)t->xs_ld * (maxn / t->gs) * sizeof(float));
     if (e == cudaSuccess) e = cudaMemset(t->xq, 0, (size_t)BP * maxn);
     if (e == cudaSuccess) e = cudaMemset(t->xqs, 0, (size_t)BP * (maxn / t->gs) * sizeof(float));
     if (e == cudaSuccess) e = cudaMemset(t->xqsum, 0, (size_t)BP * (maxn / t->gs) * sizeof(int));
@@ -148,6 +156,8 @@ int alloc_state(Transformer* t) {
     return LQ_OK;
 }
 
+bool use_mma(const Transformer* t, int batch) { return batch >= t->mma_min; }
+
 // release the per-sequence state (activations, caches, host mirrors, graph)
 void free_state(Transformer* t) {
     if (t->stream) cudaStreamSynchronize(t->stream);
@@ -157,8 +167,10 @@ void free_state(Transformer* t) {
     t->graph = nullptr;
     t->graph_batch = 0;
     void* bufs[] = {t->x, t->q, t->att, t->h1, t->h3, t->xq, t->xqs, t->xqsum, t->logits, t->kc, t->vc,
-                    t->part, t->counters, t->meta, t->next, t->err, t->rope};
+                    t->part, t->counters, t->meta, t->next, t->err, t->rope, t->xs_t, t->qg_part, t->qg_cnt};
     for (void* b : bufs) cudaFree(b);
+    t->xs_t = t->qg_part = nullptr;
+    t->qg_cnt = nullptr;
     t->x = t->q = t->att = t->h1 = t->h3 = t->logits = t->kc = t->vc = t->part = nullptr;
     t->xq = nullptr;
     t->xqs = nullptr;
@@ -182,6 +194,35 @@ int gemv_chunk(int cols) {
 
 // One GEMV over `batch` activation rows: launches of up to gemv_chunk rows,
 // the last one rounded up to a kernel row count with the extra rows unstored.
+cudaError_t gemv_rows(const GemvArgs& a, int kind, int batch, cudaStream_t st, int num_sms);
+
+// The product of one decode stage for `batch` activation rows: from
+// t->mma_min rows on, on the tensor cores (up to 64 rows per launch), else
+// the GEMV.
+cudaError_t product_rows(Transformer* t, const GemvArgs& a, int batch, cudaStream_t st) {
+    const int kind = t->kind;
+    if (use_mma(t, batch) && qgemm_ok(a, kind, batch < 64 ? batch : 64) && qgemm_max_tiles(a) <= kQgTiles) {
+        const int ng = a.cols / a.gs;
+        for (int b0 = 0; b0 < batch; b0 += 64) {
+            const int rows = batch - b0 < 64 ? batch - b0 : 64;
+            GemvArgs c = a;
+            c.nb = c.nvalid = rows;
+            c.xq = a.xq + (size_t)b0 * a.cols;
+            c.xs = a.xs + (size_t)b0 * ng;
+            c.xsum_in = nullptr;
+            c.meta = a.meta + 2 * b0;
+            for (int i = 0; i < c.nseg; ++i)
+                if (c.seg[i].y) c.seg[i].y += (size_t)b0 * a.y_stride;
+            if (c.kcache) c.kcache += (size_t)b0 * a.kv_seq_stride;
+            if (c.vcache) c.vcache += (size_t)b0 * a.kv_seq_stride;
+            cudaError_t e = qgemm_launch(c, kind, t->xs_t + b0, t->xs_ld, t->qg_part, t->qg_cnt, st, true, t->num_sms);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    }
+    return gemv_rows(a, kind, batch, st, t->num_sms);
+}
+
 cudaError_t gemv_rows(const GemvArgs& a, int kind, int batch, cudaStream_t st, int num_sms) {
     const int chunk = gemv_chunk(a.cols);
     const int ng = a.cols / a.gs;
@@ -213,6 +254,10 @@ Transformer* new_transformer(const Config* c, int kind, int gs, int max_seq, int
     t->gs = gs;
     t->max_seq = (max_seq > 0 && max_seq < c->seq_len) ? max_seq : c->seq_len;
     t->max_batch = max_batch;
+    if (const char* e = getenv("LQ_MMA_MIN_ROWS")) {
+        t->mma_min = atoi(e);
+        if (t->mma_min < 1) t->mma_min = 1 << 30;  // 0 or negative: never
+    }
     cudaGetDevice(&t->dev);
     cudaDeviceGetAttribute(&t->num_sms, cudaDevAttrMultiProcessorCount, t->dev);
     return t;
@@ -261,6 +306,11 @@ int forward_launch(Transformer* t, int batch) {
         q.xq = t->xq;
         q.xs = t->xqs;
         q.xsum = t->xqsum;
+        if (use_mma(t, batch)) {
+            q.xs_t = t->xs_t;
+            q.npad = t->xs_ld;
+            q.xs_t_mul = kind == LQ_KIND_INT4 ? 0.0625f : 1.0f;
+        }
         return act_quant_launch(q, st, true);
     };
     auto qin = [&](GemvArgs& a) {
@@ -282,7 +332,7 @@ int forward_launch(Transformer* t, int batch) {
         qin(a);
         a.kcache = t->kc + l * kv_layer;
         a.vcache = t->vc + l * kv_layer;
-        if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
+        if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
         // 2. attention
         AttnArgs at{};
         at.q = t->q;
@@ -307,7 +357,7 @@ int forward_launch(Transformer* t, int batch) {
         a.seg[0] = {t->wo.q + (size_t)l * D * rbD, t->wo.s + (size_t)l * D * ngD, t->x, D, EPI_ADD};
         a.nseg = 1;
         qin(a);
-        if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "wo gemv");
+        if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "wo gemv");
         // 4. w1 | w3 paired, SwiGLU in the epilogue: h1 = silu(x.w1) * (x.w3)
         if ((e = quant(IN_RMSNORM, t->x, D, t->rms_ffn + (size_t)l * D)) != cudaSuccess)
             return cuda_fail(e, "ffn rmsnorm");
@@ -318,14 +368,14 @@ int forward_launch(Transformer* t, int batch) {
         a.paired = 1;
         a.y_stride = H;
         qin(a);
-        if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w1/w3 gemv");
+        if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "w1/w3 gemv");
         // 5. w2 + residual
         if ((e = quant(IN_F32, t->h1, H, nullptr)) != cudaSuccess) return cuda_fail(e, "ffn quantize");
         base(a, H);
         a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->x, D, EPI_ADD};
         a.nseg = 1;
         qin(a);
-        if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
+        if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
     }
     GemvArgs a;
     if ((e = quant(IN_RMSNORM, t->x, D, t->rms_final)) != cudaSuccess) return cuda_fail(e, "final rmsnorm");
@@ -334,13 +384,17 @@ int forward_launch(Transformer* t, int batch) {
     a.nseg = 1;
     a.y_stride = c.vocab_size;
     qin(a);
-    if ((e = gemv_rows(a, kind, batch, st, t->num_sms)) != cudaSuccess) return cuda_fail(e, "classifier gemv");
+    if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "classifier gemv");
     if ((e = argmax_launch(t->logits, c.vocab_size, batch, c.vocab_size, t->next, st, true)) != cudaSuccess)
         return cuda_fail(e, "argmax");
     return LQ_OK;
 }
 
 int kernels_per_step(const Transformer* t, int batch) {
+    if (use_mma(t, batch)) {
+        const int g = (batch + 63) / 64;
+        return t->c.n_layers * (5 + 4 * g) + 2 + g;
+    }
     const int cd = gemv_chunk(t->c.dim), ch = gemv_chunk(t->c.hidden_dim);
     const int gd = (batch + cd - 1) / cd, gh = (batch + ch - 1) / ch;
     // per layer: 4 quantizers, attention, GEMVs qkv / wo / w1|w3 (dim inputs) and w2 (hidden inputs)

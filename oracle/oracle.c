@@ -169,6 +169,7 @@ typedef struct {
 struct OrcModel {
     OrcConfig c;
     int kind, gs;
+    int mma_grid; /* > 0: GEMVs in the tensor-core GEMM's order for this grid size */
     float *emb, *rms_att, *rms_ffn, *rms_final;
     OrcQ wq, wk, wv, wo, w1, w2, w3, wcls;
     uint8_t* file;      /* whole file in memory */
@@ -483,10 +484,62 @@ static void mirror_act_quant(const float* x, const float* w, int n, int gs, int8
 /* kernel selection of the product's GEMV (bulk-copy kernel when every
  * segment has an even row count and the group count is a multiple of 4) */
 typedef struct {
-    int mode; /* 0: whole rows (bulk copy), 1: row slices (bulk copy), 2: plain-load kernel */
+    int mode; /* 0: whole rows (bulk copy), 1: row slices (bulk copy), 2: plain-load kernel,
+                 3: tensor-core GEMM (stream-K pieces) */
     int slice_groups;
     int lpg;  /* plain-load kernel: lanes per group */
+    int tile0, tiles, grid; /* mode 3: first tile of this matrix, tiles in the launch, CTAs */
 } RowOrder;
+
+/* stream-K partition of the tensor-core GEMM: CTA i owns stages [i*W/G, (i+1)*W/G) */
+static int64_t sk_start(int64_t i, int64_t W, int64_t G) { return i * W / G; }
+static int64_t sk_owner(int64_t s, int64_t W, int64_t G) { return ((s + 1) * G + W - 1) / W - 1; }
+
+static RowOrder mma_order(int tile0, int tiles, int grid) {
+    RowOrder o = {3, 0, 1, tile0, tiles, grid};
+    return o;
+}
+
+/* One output of the tensor-core GEMM: per piece of the row's tile, fmaf over
+ * its groups in K order from 0; pieces summed left to right. */
+static float mma_row(const int32_t* D, const float* srow, const float* xs, int n, int gs, int64_t r, RowOrder o) {
+    const int K = n / 128, gst = 128 / gs;
+    const int64_t W = (int64_t)o.tiles * K;
+    const int64_t G = W < o.grid ? W : o.grid;
+    const int64_t t = o.tile0 + r / 128, tk0 = t * K;
+    const int64_t first = sk_owner(tk0, W, G), last = sk_owner(tk0 + K - 1, W, G);
+    float y = 0.0f;
+    for (int64_t i = first; i <= last; i++) {
+        int64_t k0 = sk_start(i, W, G), k1 = sk_start(i + 1, W, G);
+        if (k0 < tk0) k0 = tk0;
+        if (k1 > tk0 + K) k1 = tk0 + K;
+        float acc = 0.0f;
+        for (int64_t g = (k0 - tk0) * gst; g < (k1 - tk0) * gst; g++) acc = fmaf(srow[g] * xs[g], (float)D[g], acc);
+        y = i == first ? acc : y + acc;
+    }
+    return y;
+}
+
+void orc_gemm_mma(float* out, const int8_t* xq, const float* xs, const uint8_t* wq, const float* ws, int B,
+                  int64_t rows, int64_t n, int gs, int kind, int tile0, int tiles, int grid) {
+    const int ng = (int)(n / gs);
+    const size_t rb = kind == 8 ? (size_t)n : (size_t)n / 2;
+    int32_t* D = (int32_t*)malloc(sizeof(int32_t) * ng);
+    RowOrder o = mma_order(tile0, tiles, grid);
+    for (int b = 0; b < B; b++)
+        for (int64_t r = 0; r < rows; r++) {
+            for (int g = 0; g < ng; g++) {
+                int32_t d = 0;
+                for (int j = 0; j < gs; j++)
+                    d += wval(wq + r * rb, (int64_t)g * gs + j, kind) * (int32_t)xq[(size_t)b * n + g * gs + j];
+                D[g] = d;
+            }
+            out[(size_t)b * rows + r] = mma_row(D, ws + r * ng, xs + (size_t)b * ng, (int)n, gs, r, o);
+        }
+    free(D);
+}
+
+void orc_set_mma_grid(OrcModel* m, int grid) { m->mma_grid = grid; }
 
 static RowOrder row_order(int n, int gs, int kind, int paired, int rows_even) {
     RowOrder o = {0, 0, 1};
@@ -504,8 +557,17 @@ static RowOrder row_order(int n, int gs, int kind, int paired, int rows_even) {
 }
 
 static float mirror_row(const uint8_t* wrow, const float* srow, const int8_t* xq, const float* xs, int n, int gs,
-                        int kind, RowOrder o) {
+                        int kind, RowOrder o, int64_t r) {
     int ng = n / gs;
+    if (o.mode == 3) {
+        int32_t D[1024];
+        for (int g = 0; g < ng; g++) {
+            int32_t d = 0;
+            for (int j = 0; j < gs; j++) d += wval(wrow, (int64_t)g * gs + j, kind) * (int32_t)xq[g * gs + j];
+            D[g] = d;
+        }
+        return mma_row(D, srow, xs, n, gs, r, o);
+    }
     float lanes[32] = {0};
     float tmp[32];
     for (int g = 0; g < ng; g++) {
@@ -533,7 +595,7 @@ static void mirror_gemv(float* out, const OrcQ* w, int64_t l, int64_t rows, cons
     size_t rb = row_bytes(n, kind);
     const uint8_t* q = w->q + (size_t)l * rows * rb;
     const float* s = w->s + (size_t)l * rows * (n / gs);
-    for (int64_t r = 0; r < rows; r++) out[r] = mirror_row(q + r * rb, s + r * (n / gs), xq, xs, n, gs, kind, o);
+    for (int64_t r = 0; r < rows; r++) out[r] = mirror_row(q + r * rb, s + r * (n / gs), xq, xs, n, gs, kind, o, r);
 }
 
 /* attention of one head over positions 0..pos in chunks of 64 (kernel order) */
@@ -609,14 +671,26 @@ float* orc_forward_kernel_order(OrcModel* m, int token, int pos) {
     RowOrder o_ffn = row_order(dim, gs, kind, 1, hidden % 2 == 0);
     RowOrder o_w2 = row_order(hidden, gs, kind, 0, dim % 2 == 0);
     RowOrder o_cls = row_order(dim, gs, kind, 0, p->vocab_size % 2 == 0);
+    RowOrder o_q = o_dim, o_k = o_dim, o_v = o_dim;
+    if (m->mma_grid > 0) {
+        /* batched steps: every product on the tensor-core GEMM (qkv is one launch of three matrices) */
+        int tq = dim / 128, tkv = kv_dim / 128, G = m->mma_grid;
+        o_q = mma_order(0, tq + 2 * tkv, G);
+        o_k = mma_order(tq, tq + 2 * tkv, G);
+        o_v = mma_order(tq + tkv, tq + 2 * tkv, G);
+        o_wo = mma_order(0, dim / 128, G);
+        o_ffn = mma_order(0, hidden / 128, G);
+        o_w2 = mma_order(0, dim / 128, G);
+        o_cls = mma_order(0, p->vocab_size / 128, G);
+    }
     for (int64_t l = 0; l < p->n_layers; l++) {
         size_t loff = (size_t)l * m->max_seq * kv_dim;
         float* k = m->kc + loff + (size_t)pos * kv_dim;
         float* v = m->vc + loff + (size_t)pos * kv_dim;
         mirror_act_quant(x, m->rms_att + l * dim, dim, gs, m->aq, m->as, tmp);    /* runq.c:338,345 */
-        mirror_gemv(m->q, &m->wq, l, dim, m->aq, m->as, dim, gs, kind, o_dim);      /* :346-348 */
-        mirror_gemv(k, &m->wk, l, kv_dim, m->aq, m->as, dim, gs, kind, o_dim);
-        mirror_gemv(v, &m->wv, l, kv_dim, m->aq, m->as, dim, gs, kind, o_dim);
+        mirror_gemv(m->q, &m->wq, l, dim, m->aq, m->as, dim, gs, kind, o_q);        /* :346-348 */
+        mirror_gemv(k, &m->wk, l, kv_dim, m->aq, m->as, dim, gs, kind, o_k);
+        mirror_gemv(v, &m->wv, l, kv_dim, m->aq, m->as, dim, gs, kind, o_v);
         for (int i = 0; i < dim; i += 2) {                                          /* RoPE :351-365 */
             int hd = i % hs;
             float freq = 1.0f / powf(10000.0f, hd / (float)hs);

@@ -70,6 +70,13 @@ float* orc_forward(OrcModel* m, int token, int pos);
  * product.  Uses the model's own KV cache: do not mix with orc_forward on
  * one model. */
 float* orc_forward_kernel_order(OrcModel* m, int token, int pos);
+/* grid > 0: orc_forward_kernel_order mirrors the batched step, whose products
+ * run on the tensor-core GEMM with `grid` CTAs (stream-K order); 0: batch-1 GEMV */
+void orc_set_mma_grid(OrcModel* m, int grid);
+/* the tensor-core GEMM's fp32 order for one matrix of a launch: rows of tiles
+ * tile0.. of a launch of `tiles` 128-row tiles over `grid` CTAs */
+void orc_gemm_mma(float* out, const int8_t* xq, const float* xs, const uint8_t* wq, const float* ws, int B,
+                  int64_t rows, int64_t n, int gs, int kind, int tile0, int tiles, int grid);
 /* exp as evaluated by the product (Cody-Waite + Taylor degree 7). */
 float orc_expf(float x);
 /* sample_argmax, runq.c:578-585: first index of the maximum. */

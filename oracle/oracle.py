@@ -46,6 +46,8 @@ def orc() -> C.CDLL:
         L.orc_argmax.argtypes = [_P, I]
         L.orc_forward_kernel_order.restype = C.POINTER(C.c_float)
         L.orc_forward_kernel_order.argtypes = [_P, I, I]
+        L.orc_gemm_mma.argtypes = [_P, _P, _P, _P, _P, I, I64, I64, I, I, I, I, I]
+        L.orc_set_mma_grid.argtypes = [_P, I]
         L.orc_expf.restype = C.c_float
         L.orc_expf.argtypes = [C.c_float]
         _orc = L
@@ -118,6 +120,21 @@ def gemv(xq, xs, wq, ws, cols: int, gs: int, kind: int) -> np.ndarray:
     return out
 
 
+def gemm_mma(xq, xs, wq, ws, cols: int, gs: int, kind: int, tile0: int = 0, tiles: int = 0,
+             grid: int = 148) -> np.ndarray:
+    """The tensor-core GEMM's fp32 order: out [B, rows] for rows of tiles
+    tile0.. of a launch of `tiles` 128-row tiles on `grid` CTAs."""
+    xq = np.ascontiguousarray(np.atleast_2d(xq))
+    xs = np.ascontiguousarray(np.atleast_2d(xs), dtype=np.float32)
+    rows = wq.shape[0]
+    B = xq.shape[0]
+    tiles = tiles or rows // 128
+    out = np.empty((B, rows), np.float32)
+    orc().orc_gemm_mma(_ptr(out), _ptr(xq), _ptr(xs), _ptr(np.ascontiguousarray(wq)),
+                       _ptr(np.ascontiguousarray(ws, dtype=np.float32)), B, rows, cols, gs, kind, tile0, tiles, grid)
+    return out
+
+
 class OracleModel:
     """Scalar CPU forward (runq.c:320-421 with INT4 and GS as parameters)."""
 
@@ -135,6 +152,11 @@ class OracleModel:
     def forward(self, token: int, pos: int) -> np.ndarray:
         p = orc().orc_forward(self.h, token, pos)
         return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def set_mma_grid(self, grid: int) -> None:
+        """grid > 0: forward_kernel_order mirrors a batched step (products on
+        the tensor-core GEMM with `grid` CTAs); 0: the batch-1 GEMV."""
+        orc().orc_set_mma_grid(self.h, grid)
 
     def forward_kernel_order(self, token: int, pos: int) -> np.ndarray:
         """The step in the product kernels' fp32 reduction order."""

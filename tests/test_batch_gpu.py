@@ -122,3 +122,32 @@ def test_batch_errors(cuda):
     t.reserve_batch(2)
     assert t.forward_batch([1, 2], [0, 0]).shape == (2, synth.SMALL64_CONFIG[5])
     t.close()
+
+
+@pytest.mark.parametrize("kind,batch", [(8, 16), (4, 20)])
+def test_tensor_core_batch_bit_exact_vs_oracle(cuda, kind, batch):
+    """From 16 sequences on, every product of the step runs on the tensor
+    cores (tcgen05 kind::i8); each row equals the oracle's restatement of
+    that order for its own sequence, bit for bit."""
+    import oracle as O
+
+    conf = synth.SMALL64_CONFIG
+    path = synth.tiny_checkpoint(kind, 64, config=conf)
+    t = lq.Transformer.from_file(path, 64)
+    t.reserve_batch(batch)
+    rng = np.random.default_rng(batch + kind)
+    steps = 12
+    hist = rng.integers(0, conf[5], size=(batch, steps))
+    got = []
+    for p in range(steps):
+        got.append(t.forward_batch(hist[:, p], np.full(batch, p, np.int32)).copy())
+    t.close()
+    sms = cuda.cuda.get_device_properties(0).multi_processor_count
+    M = O.OracleModel(path, 64)
+    M.set_mma_grid(sms)
+    for b in range(batch):
+        for p in range(steps):
+            lo = M.forward_kernel_order(int(hist[b, p]), p)
+            g = got[p][b]
+            assert np.array_equal(g.view(np.uint32), lo.view(np.uint32)), (b, p, float(np.abs(g - lo).max()))
+    M.close()

@@ -112,3 +112,45 @@ def test_kernel_order_oracle_tracks_runq(golden):
         assert float(np.abs(lo - g[f"logits_{pos}"]).max() / np.abs(g[f"logits_{pos}"]).max()) < 1e-5
         token = int(stream[pos])
     M.close()
+
+
+@pytest.mark.parametrize("kind,gs", [(8, 64), (4, 64), (8, 32), (4, 128)])
+def test_tensor_core_order_restatement(kind, gs):
+    """The oracle's restatement of the tensor-core GEMM's fp32 order (stream-K
+    pieces over a launch) is a reordering of the same terms as the plain
+    GEMV: within the rigorous reordering bound of it, for every partition."""
+    rng = np.random.default_rng(gs + kind)
+    d, n, B = 384, 1024, 3
+    w = (rng.standard_normal((d, n)) * 0.02).astype(np.float32)
+    wq, ws = O.quantize_weight(w, gs, kind)
+    x = rng.standard_normal((B, n)).astype(np.float32)
+    xq, xs, _ = O.quantize_act(x, gs)
+    plain = O.gemv(xq, xs, wq, ws, n, gs, kind)
+    D = np.stack([O.group_dots(wq, xq[b], n, gs, kind) for b in range(B)]).astype(np.float64)
+    bound = 2 * (n // gs) * np.finfo(np.float32).eps * np.abs(ws[None] * xs[:, None, :] * D).sum(-1)
+    outs = set()
+    for tile0, tiles, grid in [(0, 3, 1), (0, 3, 2), (0, 3, 5), (0, 3, 24), (2, 9, 7), (0, 3, 148)]:
+        got = O.gemm_mma(xq, xs, wq, ws, n, gs, kind, tile0, tiles, grid)
+        assert np.all(np.abs(got - plain) <= bound + 1e-30)
+        outs.add(got.tobytes())
+    assert len(outs) > 1  # the partition does change the fp32 order
+
+
+def test_tensor_core_order_single_piece_is_sequential():
+    """One CTA per tile (grid = tiles): each output is fmaf over its groups in
+    K order from 0, restated here with numpy (product exact in float64, one
+    rounding to float32)."""
+    rng = np.random.default_rng(3)
+    d, n, gs = 128, 512, 64
+    w = (rng.standard_normal((d, n)) * 0.02).astype(np.float32)
+    wq, ws = O.quantize_weight(w, gs, 8)
+    x = rng.standard_normal((1, n)).astype(np.float32)
+    xq, xs, _ = O.quantize_act(x, gs)
+    got = O.gemm_mma(xq, xs, wq, ws, n, gs, 8, 0, 1, 1)[0]
+    D = O.group_dots(wq, xq[0], n, gs, 8)
+    for r in range(0, d, 17):
+        acc = np.float32(0)
+        for g in range(n // gs):
+            f = np.float32(ws[r, g] * xs[0, g])
+            acc = np.float32(np.float64(f) * np.float64(D[r, g]) + np.float64(acc))
+        assert got[r] == acc, r
