@@ -921,7 +921,10 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_cons
         const int g = task / lpg;
         a.xs[(size_t)b * ng + g] = sc;
         a.xsum[(size_t)b * ng + g] = qs;
-        if (a.xs_t) a.xs_t[(size_t)g * a.npad + b] = sc * a.xs_t_mul;
+        if (a.xs_t) {
+            const int c = b >> 6, ld = c < a.xs_nfull ? 64 : a.xs_npad_last;
+            a.xs_t[(size_t)c * ng * 64 + (size_t)g * ld + (b & 63)] = sc * a.xs_t_mul;
+        }
     }
 }
 

@@ -105,10 +105,12 @@ struct ActQuantArgs {
     int8_t* xq;
     float* xs;
     int* xsum;
-    // optional (tensor-core GEMM input): scales transposed to [n/gs][npad],
+    // optional (tensor-core GEMM input): scales transposed per chunk of 64
+    // rows, chunk c at xs_t + c * (n/gs) * 64 as [n/gs][npad_c] with npad_c =
+    // 64 for the first xs_nfull chunks and xs_npad_last for the last one;
     // multiplied by xs_t_mul (1, or 1/16 for int4 weights held as 16*q)
     float* xs_t;
-    int npad;
+    int xs_nfull, xs_npad_last;
     float xs_t_mul;
 };
 cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl);

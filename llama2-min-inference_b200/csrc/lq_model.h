@@ -43,8 +43,8 @@ struct Transformer {
     float2* rope = nullptr;              // [max_seq][head_size/2] cos/sin table
     // tensor-core GEMM path (steps of mma_min or more sequences)
     int mma_min = 16;
-    int xs_ld = 0;                       // leading dimension of xs_t (max_batch rounded up to 64)
-    float* xs_t = nullptr;               // activation scales transposed [max groups][xs_ld]
+    int xs_ld = 0;                       // max_batch rounded up to 64 (xs_t: a [groups][64] table per 64 rows)
+    float* xs_t = nullptr;               // activation scales transposed, per chunk of 64 rows
     float* qg_part = nullptr;            // stream-K partials
     int* qg_cnt = nullptr;               // per-tile arrival counters
     // pinned host mirrors

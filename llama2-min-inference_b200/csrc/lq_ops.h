@@ -17,6 +17,7 @@ struct AttnArgs {
     float* part;         // [batch][n_heads][max_splits][head_size + 2] partials
     int* counters;       // [batch][n_kv_heads], zero between steps
     const int* meta;     // [batch][token, pos]
+    int* err;            // device error word (a bounded wait that gave up)
     int64_t kv_seq_stride;
     int q_stride;
     int n_heads, n_kv_heads, kv_mul, head_size, max_seq, max_splits;

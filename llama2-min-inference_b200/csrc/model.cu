@@ -215,7 +215,9 @@ cudaError_t product_rows(Transformer* t, const GemvArgs& a, int batch, cudaStrea
                 if (c.seg[i].y) c.seg[i].y += (size_t)b0 * a.y_stride;
             if (c.kcache) c.kcache += (size_t)b0 * a.kv_seq_stride;
             if (c.vcache) c.vcache += (size_t)b0 * a.kv_seq_stride;
-            cudaError_t e = qgemm_launch(c, kind, t->xs_t + b0, t->xs_ld, t->qg_part, t->qg_cnt, st, true, t->num_sms);
+            // this chunk's scale table: [ng][npad] at chunk offset ng * 64
+            cudaError_t e = qgemm_launch(c, kind, t->xs_t + (size_t)(b0 / 64) * ng * 64, qgemm_npad(rows), t->qg_part,
+                                         t->qg_cnt, st, true, t->num_sms);
             if (e != cudaSuccess) return e;
         }
         return cudaSuccess;
@@ -308,7 +310,8 @@ int forward_launch(Transformer* t, int batch) {
         q.xsum = t->xqsum;
         if (use_mma(t, batch)) {
             q.xs_t = t->xs_t;
-            q.npad = t->xs_ld;
+            q.xs_nfull = batch / 64;
+            q.xs_npad_last = batch % 64 ? qgemm_npad(batch % 64) : 64;
             q.xs_t_mul = kind == LQ_KIND_INT4 ? 0.0625f : 1.0f;
         }
         return act_quant_launch(q, st, true);
@@ -342,6 +345,7 @@ int forward_launch(Transformer* t, int batch) {
         at.part = t->part;
         at.counters = t->counters;
         at.meta = t->meta;
+        at.err = t->err;
         at.kv_seq_stride = kv_seq;
         at.q_stride = D;
         at.n_heads = c.n_heads;

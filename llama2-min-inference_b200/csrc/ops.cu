@@ -59,12 +59,14 @@ cudaError_t quantize_act_launch(const float* x, int64_t rows, int64_t n, int gs,
 
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnArgs a) {
     extern __shared__ __align__(16) float asmem[];
+    __shared__ __align__(8) uint64_t kv_bar;
     pdl_trigger();
     const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
     const int hs = a.head_size, km = a.kv_mul;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     constexpr int NW = kAttnThreads / 32;
-    pdl_wait();
+    // the positions were written before the step's first kernel started, so
+    // they can be read before waiting for the preceding kernel
     const int pos = a.meta[2 * b + 1];
     const int nsplit = pos / kChunk + 1;
     if (split >= nsplit) return;
@@ -77,17 +79,30 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     float* sc = qs + km * hs;           // [km][kChunk]
     float* ml = sc + km * kChunk;       // [km][2]
 
+    // K and V of the chunk by two bulk copies (TMA).  A chunk without the
+    // current position holds only earlier steps' keys and values, so its copy
+    // starts before the preceding kernel (which writes position pos) is done.
     const size_t cbase = (size_t)b * a.kv_seq_stride + ((size_t)kvh * a.max_seq + t0) * hs;
-    const float4* kg = reinterpret_cast<const float4*>(a.kcache + cbase);
-    const float4* vg = reinterpret_cast<const float4*>(a.vcache + cbase);
-    const int n4 = nt * hs / 4;
-    for (int i = tid; i < n4; i += kAttnThreads) {
-        reinterpret_cast<float4*>(ks)[i] = kg[i];
-        reinterpret_cast<float4*>(vs)[i] = vg[i];
+    const uint32_t bytes = (uint32_t)(nt * hs * sizeof(float));
+    if (tid == 0) {
+        mbar_init(&kv_bar, 1);
+        fence_mbar_init();
+        if (t0 + nt - 1 == pos) pdl_wait();
+        const uint64_t pol = l2_evict_first_policy();
+        mbar_arrive_expect_tx(&kv_bar, 2 * bytes);
+        bulk_g2s(ks, a.kcache + cbase, bytes, &kv_bar, pol);
+        bulk_g2s(vs, a.vcache + cbase, bytes, &kv_bar, pol);
     }
+    pdl_wait();
     const float* qg = a.q + (size_t)b * a.q_stride + (size_t)kvh * km * hs;
     for (int i = tid; i < km * hs; i += kAttnThreads) qs[i] = qg[i];
-    __syncthreads();
+    __syncthreads();  // also orders the barrier's initialisation before the waits below
+    const bool landed = mbar_wait(&kv_bar, 0, a.err, DEV_TIMEOUT_FULL);
+    if (!__syncthreads_and(landed)) {
+        // give up on this chunk; confirm the copies before the CTA's shared memory is released
+        if (tid == 0) mbar_wait(&kv_bar, 0, a.err, DEV_TIMEOUT_DRAIN);
+        return;
+    }
 
     // scores: warp per position, lanes over dims
     const float rs = sqrtf((float)hs);

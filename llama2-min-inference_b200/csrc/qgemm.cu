@@ -10,7 +10,7 @@
 // The per-group int32 dots are exact; the fp32 epilogue is
 // acc = fmaf(ws * xs, (float)D, acc) over the groups in K order.
 //
-// One persistent CTA per SM, warp-specialised (448 threads):
+// One persistent CTA per SM, warp-specialised (704 threads):
 //   warp 0       TMA producer: per stage (128 bytes of K) the weight tile of
 //                128 rows (128 bytes, or the 64 packed bytes of INT4) and the
 //                activation tile (npad rows x 128 bytes), 2-D tensor maps
@@ -24,7 +24,7 @@
 //                INT4 nibbles become s8 bytes holding 16*q (the nibble in the
 //                high half), so D comes out as 16*D and the activation scale
 //                table carries xs/16 (both scalings are exact)
-//   warps 6-13   epilogue: per group, tcgen05.ld of the int32 dots (TMEM lane
+//   warps 6-21   epilogue: per group, tcgen05.ld of the int32 dots (TMEM lane
 //                = weight row, column = activation row), exact int->float via
 //                the 1.5*2^23 bias (|D| < 2^22), packed fp32x2 scale and fma
 // Work split: stream-K over the sequence of (tile, stage) pairs of the whole
@@ -51,13 +51,17 @@ namespace lq {
 
 namespace {
 
-constexpr int kQgThreads = 448;
+constexpr int kMmaWarp0 = 1;
+constexpr int kMmaWarps = 2;     // MMA-issuing warps, taking turns by stage
+constexpr int kConvWarp0 = kMmaWarp0 + kMmaWarps;
+constexpr int kQgThreads = 32 * (kConvWarp0 + 4 + 16);
 constexpr int kTileRows = 128;   // MMA M: weight rows per tile
 constexpr int kStageK = 128;     // K bytes (int8 elements) per stage
-constexpr int kNBuf = 4;         // TMEM group-accumulator ring depth
+constexpr int kMaxBuf = 8;       // TMEM group-accumulator ring: 8 / MULT buffers
 constexpr int kConvWarps = 4;
-constexpr int kEpiWarps = 8;
-constexpr int kEpiWarp0 = 6;
+constexpr int kEpiWarps = 16;
+constexpr int kEpiWarp0 = kConvWarp0 + kConvWarps;
+constexpr int kXsStages = 8;     // activation-scale ring: one entry (the stage's groups) per stage
 
 enum : int {
     DEV_TIMEOUT_CONV = 0x111,   // MMA waited too long for a converted stage
@@ -124,6 +128,13 @@ template <int NC>
 __device__ __forceinline__ void tmem_ld(uint32_t taddr, int (&d)[NC]);
 
 template <>
+__device__ __forceinline__ void tmem_ld<4>(uint32_t taddr, int (&d)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+                 : "r"(taddr));
+}
+
+template <>
 __device__ __forceinline__ void tmem_ld<8>(uint32_t taddr, int (&d)[8]) {
     asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                  : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]),
@@ -185,14 +196,27 @@ __device__ __host__ __forceinline__ int sk_owner(int64_t s, int64_t W, int G) {
 }
 
 struct Bars {
-    uint64_t full[16], conv[16], empty[16], tfull[kNBuf], tempty[kNBuf], done;
+    uint64_t full[16], conv[16], empty[16], tfull[kMaxBuf], tempty[kMaxBuf], done[kMmaWarps];
+    uint64_t xfull[kXsStages], xempty[kXsStages];
     uint32_t tmem_base;
     int abort_flag;
     int last_flag;
 };
 
 // wait that returns at once when the CTA has given up; records `code` on timeout
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
 __device__ __forceinline__ bool qwait(uint64_t* bar, uint32_t parity, int* err, int code, volatile int* abort_flag) {
+    if (mbar_test_wait(bar, parity)) return true;  // already complete: no blocking probe
     if (*abort_flag) return false;
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = globaltimer();
@@ -216,21 +240,34 @@ struct Layout {
     static constexpr int kB = N * kStageK;                 // activation tile
     static constexpr int kStage = MULT * (kA + kP) + kB;   // multiple of 1024
     static constexpr uint32_t kTx = MULT * (KIND == 4 ? kP : kA) + kB;
+    static constexpr int kNBuf = 8 / MULT;                 // TMEM group buffers (8 * N columns in all)
+    static constexpr int kXsEntry = 4 * N * 4;             // activation scales of one stage (up to 4 groups)
+    static constexpr int kXs = kXsStages * kXsEntry;       // activation-scale ring
 };
+
+// the epilogue of one finished row pair, out of line: it runs once per tile
+// and column, and inlining all its cases would crowd the group loop's registers
+__device__ __noinline__ void finish_pair(const GemvArgs& a, const GemvSeg& g, int b, int r, float v0, float v1,
+                                         float u0, float u1) {
+    finish_rows(a, g, b, r, v0, v1, u0, u1, true);
+}
 
 template <int KIND, int N, int MULT>
 __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_constant__ QgemmArgs a) {
     using Lay = Layout<KIND, N, MULT>;
+    constexpr int kNBuf = Lay::kNBuf;
     extern __shared__ __align__(1024) unsigned char qsm_raw[];
     unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(qsm_raw) + 1023) & ~(uintptr_t)1023);
     const int S = a.stages;
-    Bars* bars = reinterpret_cast<Bars*>(sm + (size_t)S * Lay::kStage);
+    float* xring = reinterpret_cast<float*>(sm + (size_t)S * Lay::kStage);
+    Bars* bars = reinterpret_cast<Bars*>(sm + (size_t)S * Lay::kStage + Lay::kXs);
     volatile int* abort_flag = &bars->abort_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int G = gridDim.x;
     const int K = a.kst;
     const int64_t W = (int64_t)a.tiles * K;
     const int64_t s0 = sk_start(blockIdx.x, W, G), s1 = sk_start(blockIdx.x + 1, W, G);
+    const int nst = (int)(s1 - s0);  // this CTA's stages
     const int gs = a.ep.gs, gst = kStageK / gs;  // groups per stage
     const int ng = a.ep.cols / gs;
     int* err = a.ep.err;
@@ -249,13 +286,17 @@ __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_const
             mbar_init(&bars->tfull[i], 1);
             mbar_init(&bars->tempty[i], kEpiWarps);
         }
-        mbar_init(&bars->done, 1);
+        for (int i = 0; i < kXsStages; ++i) {
+            mbar_init(&bars->xfull[i], 1);
+            mbar_init(&bars->xempty[i], kEpiWarps);
+        }
+        for (int i = 0; i < kMmaWarps; ++i) mbar_init(&bars->done[i], 1);
         bars->abort_flag = 0;
         bars->last_flag = 0;
         fence_mbar_init();
     }
     constexpr int kCols = (kNBuf * N * MULT) < 32 ? 32 : (kNBuf * N * MULT);
-    if (warp == 1) {
+    if (warp == kMmaWarp0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_addr(&bars->tmem_base)),
                      "r"(kCols)
@@ -271,90 +312,122 @@ __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_const
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            const uint64_t pw = l2_evict_first_policy(), px = l2_evict_last_policy();
-            int64_t it = 0;
-            for (int64_t s = s0; s < s1; ++s, ++it) {
-                const int slot = (int)(it % S);
-                const uint32_t ph = (uint32_t)((it / S) & 1);
-                if (!qwait(&bars->empty[slot], ph ^ 1u, err, DEV_TIMEOUT_EMPTY, abort_flag)) break;
-                const int t = (int)(s / K), k = (int)(s % K);
-                int seg = 0;
-                while (seg + 1 < a.ep.nseg && t >= a.tile_start[seg + 1]) ++seg;
-                const int row0 = (t - a.tile_start[seg]) * kTileRows;
-                mbar_arrive_expect_tx(&bars->full[slot], Lay::kTx);
-#pragma unroll
-                for (int m = 0; m < MULT; ++m) {
-                    void* dst = KIND == 4 ? (void*)tileP(slot, m) : (void*)tileA(slot, m);
-                    tma_load_2d(dst, &a.wmap[seg][m], KIND == 4 ? k * (kStageK / 2) : k * kStageK, row0,
-                                &bars->full[slot], pw);
-                }
+        // Lanes 0 and 1 wait for the stage slot and the scale-ring entry; then
+        // one lane per copy issues it (weight tile per tensor, activation
+        // tile, the stage's activation scales), so the copies start together.
+        // Counters advance incrementally: no division in the loop.
+        const uint64_t pw = l2_evict_first_policy(), px = l2_evict_last_policy();
+        int slot = 0, xslot = 0;
+        uint32_t ph = 0, xph = 0;
+        int t = (int)(s0 / K), k = (int)(s0 % K);
+        int seg = 0;
+        while (seg + 1 < a.ep.nseg && t >= a.tile_start[seg + 1]) ++seg;
+        int issued = 0;
+        for (; issued < nst; ++issued) {
+            bool ok = true;
+            if (lane == 0) ok = qwait(&bars->empty[slot], ph ^ 1u, err, DEV_TIMEOUT_EMPTY, abort_flag);
+            if (lane == 1) ok = qwait(&bars->xempty[xslot], xph ^ 1u, err, DEV_TIMEOUT_EMPTY, abort_flag);
+            if (!__all_sync(0xffffffffu, ok)) break;
+            const int row0 = (t - a.tile_start[seg]) * kTileRows;
+            if (lane == 0) mbar_arrive_expect_tx(&bars->full[slot], Lay::kTx);
+            if (lane == 1) mbar_arrive_expect_tx(&bars->xfull[xslot], gst * N * 4);
+            __syncwarp();
+            if (lane < MULT) {
+                void* dst = KIND == 4 ? (void*)tileP(slot, lane) : (void*)tileA(slot, lane);
+                tma_load_2d(dst, &a.wmap[seg][lane], KIND == 4 ? k * (kStageK / 2) : k * kStageK, row0,
+                            &bars->full[slot], pw);
+            } else if (lane == MULT) {
                 tma_load_2d(tileB(slot), &a.xmap, k * kStageK, 0, &bars->full[slot], px);
+            } else if (lane == MULT + 1) {
+                // scales of the stage's groups: contiguous in the table (row pitch = npad)
+                bulk_g2s(xring + xslot * (Lay::kXsEntry / 4), a.xs_t + (size_t)k * gst * N, gst * N * 4,
+                         &bars->xfull[xslot], px);
             }
-            // confirm the copies still in flight (only an aborted run leaves any)
-            if (*abort_flag) {
-                const int64_t issued = it;
-                for (int64_t j = issued - S; j < issued; ++j) {
-                    if (j < 0) continue;
-                    if (!mbar_wait(&bars->full[j % S], (uint32_t)((j / S) & 1), err, DEV_TIMEOUT_DRAIN)) break;
-                }
+            if (++slot == S) {
+                slot = 0;
+                ph ^= 1u;
+            }
+            if (++xslot == kXsStages) {
+                xslot = 0;
+                xph ^= 1u;
+            }
+            if (++k == K) {
+                k = 0;
+                ++t;
+                while (seg + 1 < a.ep.nseg && t >= a.tile_start[seg + 1]) ++seg;
             }
         }
-    } else if (warp == 1) {
+        // confirm the copies still in flight (only an aborted run leaves any)
+        if (lane == 0 && *abort_flag) {
+            for (int j = issued - S; j < issued; ++j) {
+                if (j < 0) continue;
+                if (!mbar_wait(&bars->full[j % S], (uint32_t)((j / S) & 1), err, DEV_TIMEOUT_DRAIN)) break;
+            }
+            for (int j = issued - kXsStages; j < issued; ++j) {
+                if (j < 0) continue;
+                if (!mbar_wait(&bars->xfull[j % kXsStages], (uint32_t)((j / kXsStages) & 1), err, DEV_TIMEOUT_DRAIN))
+                    break;
+            }
+        }
+    } else if (warp < kMmaWarp0 + kMmaWarps) {
         // ---------------- MMA issue ----------------
+        // kMmaWarps threads take turns by stage (an MMA issue costs the issuing
+        // thread more time than the tensor core needs for these small tiles).
+        // Per stage: wait for the converted operands and for the stage's last
+        // TMEM buffer (the epilogue frees buffers in order), issue the MMAs
+        // K-step-major across the stage's groups (consecutive MMAs write
+        // different accumulators when a stage holds several groups), commit
+        // each group's buffer to the epilogue and the slot to the producer.
+        const int mw = warp - kMmaWarp0;
         if (lane == 0) {
             // s32 accumulate, A s8, B s8, both K-major, N = npad, M = 128
             const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | (8u << 24);
-            int64_t it = 0, gc = 0;
+            const int ksteps = gs / 32;
+            // stage i = mw, mw + kMmaWarps, ...: slot i % S, groups i*gst .. i*gst + gst - 1
+            int slot = mw % S;
+            uint32_t ph = (uint32_t)((mw / S) & 1);
+            int gbase = mw * gst;  // first group of the stage (CTA-local)
             bool issued = false;
-            for (int64_t s = s0; s < s1 && !*abort_flag; ++s, ++it) {
-                const int slot = (int)(it % S);
-                const uint32_t ph = (uint32_t)((it / S) & 1);
+            for (int i = mw; i < nst; i += kMmaWarps) {
                 if (!qwait(&bars->conv[slot], ph, err, DEV_TIMEOUT_CONV, abort_flag)) break;
+                const int glast = gbase + gst - 1;
+                if (!qwait(&bars->tempty[glast % kNBuf], (uint32_t)(((glast / kNBuf) & 1) ^ 1), err,
+                           DEV_TIMEOUT_TEMPTY, abort_flag))
+                    break;
                 tc_fence_after();
-                bool ok = true;
+                const uint32_t abase = smem_addr(tileA(slot, 0)), bbase = smem_addr(tileB(slot));
+                for (int kk = 0; kk < ksteps; ++kk) {
+                    for (int gl = 0; gl < gst; ++gl) {
+                        const int kb = gl * gs + kk * 32;
+                        const int bb = (gbase + gl) % kNBuf;
 #pragma unroll
-                for (int j = 0; j < kStageK / 32; ++j) {
-                    const int kb = j * 32;
-                    const bool first = kb % gs == 0, last = (kb + 32) % gs == 0;
-                    const int buf = (int)(gc % kNBuf);
-                    if (first) {
-                        if (!qwait(&bars->tempty[buf], (uint32_t)(((gc / kNBuf) & 1) ^ 1), err, DEV_TIMEOUT_TEMPTY,
-                                   abort_flag)) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                    }
-#pragma unroll
-                    for (int m = 0; m < MULT; ++m) {
-                        const uint32_t d = tmem + (uint32_t)(buf * N * MULT + m * N);
-                        const uint64_t ad = smem_desc_sw128(smem_addr(tileA(slot, m)) + kb);
-                        const uint64_t bd = smem_desc_sw128(smem_addr(tileB(slot)) + kb);
-                        mma_i8(d, ad, bd, idesc, first ? 0u : 1u);
-                        issued = true;
-                    }
-                    if (last) {
-                        mma_commit(&bars->tfull[buf]);
-                        ++gc;
+                        for (int m = 0; m < MULT; ++m)
+                            mma_i8(tmem + (uint32_t)(bb * N * MULT + m * N), smem_desc_sw128(abase + m * Lay::kA + kb),
+                                   smem_desc_sw128(bbase + kb), idesc, kk > 0 ? 1u : 0u);
                     }
                 }
-                if (!ok) break;
+                issued = true;
+                for (int gl = 0; gl < gst; ++gl) mma_commit(&bars->tfull[(gbase + gl) % kNBuf]);
                 mma_commit(&bars->empty[slot]);
+                slot += kMmaWarps;
+                if (slot >= S) {
+                    slot -= S;
+                    ph ^= 1u;
+                }
+                gbase += kMmaWarps * gst;
             }
             if (issued) {
                 // every MMA this thread issued has completed before TMEM is freed
-                mma_commit(&bars->done);
-                mbar_wait(&bars->done, 0, err, DEV_TIMEOUT_MMA);
+                mma_commit(&bars->done[mw]);
+                mbar_wait(&bars->done[mw], 0, err, DEV_TIMEOUT_MMA);
             }
         }
     } else if (warp < kEpiWarp0) {
         // ---------------- operand conversion ----------------
-        const int row = threadIdx.x - 64;  // 0..127: one weight row per thread
-        int64_t it = 0;
-        for (int64_t s = s0; s < s1; ++s, ++it) {
-            const int slot = (int)(it % S);
-            const uint32_t ph = (uint32_t)((it / S) & 1);
+        const int row = threadIdx.x - kConvWarp0 * 32;  // 0..127: one weight row per thread
+        int slot = 0;
+        uint32_t ph = 0;
+        for (int i = 0; i < nst; ++i) {
             // warp-uniform decision: every lane leaves the loop together
             if (!__all_sync(0xffffffffu, qwait(&bars->full[slot], ph, err, DEV_TIMEOUT_FULL, abort_flag))) break;
 #pragma unroll
@@ -399,16 +472,21 @@ __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_const
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(&bars->conv[slot]);
+            if (++slot == S) {
+                slot = 0;
+                ph ^= 1u;
+            }
         }
     } else {
         // ---------------- epilogue ----------------
-        constexpr int NC = N / 2;  // columns per thread
+        constexpr int NC = N / (kEpiWarps / 4);  // columns per thread
         const int q = warp & 3, h = (warp - kEpiWarp0) >> 2;
         const int rr = 32 * q + lane;  // row within the tile = TMEM lane
         const int c0 = h * NC;
         const uint32_t tl = tmem + ((uint32_t)(32 * q) << 16);
         float acc[MULT][NC];
-        int64_t gc = 0;
+        int gc = 0, buf = 0, xslot = 0;
+        uint32_t bph = 0, xph = 0;
         int64_t s = s0;
         while (s < s1) {
             const int t = (int)(s / K);
@@ -417,58 +495,78 @@ __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_const
             while (seg + 1 < a.ep.nseg && t >= a.tile_start[seg + 1]) ++seg;
             const GemvSeg& sg = a.ep.seg[seg];
             const int rloc = (t - a.tile_start[seg]) * kTileRows + rr;  // row within the segment
-            const float* wsrow0 = sg.ws + (size_t)rloc * ng;
-            const float* wsrow1 = MULT == 2 ? sg.ws2 + (size_t)rloc * ng : nullptr;
+            // weight scales of this row: 16-byte loads of four groups, one quad ahead
+            const float4* wsq[MULT];
+            wsq[0] = reinterpret_cast<const float4*>(sg.ws + (size_t)rloc * ng);
+            if (MULT == 2) wsq[MULT - 1] = reinterpret_cast<const float4*>(sg.ws2 + (size_t)rloc * ng);
+            int qi = (int)((s - (int64_t)t * K) * gst) >> 2;
+            float4 wcur[MULT], wnext[MULT];
+#pragma unroll
+            for (int m = 0; m < MULT; ++m) {
+                wcur[m] = __ldg(wsq[m] + qi);
+                wnext[m] = 4 * qi + 4 < ng ? __ldg(wsq[m] + qi + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
 #pragma unroll
             for (int m = 0; m < MULT; ++m)
 #pragma unroll
                 for (int j = 0; j < NC; ++j) acc[m][j] = 0.0f;
-            for (; s < send; ++s) {
-                const int k = (int)(s % K);
+            for (int k = (int)(s - (int64_t)t * K); s < send; ++s, ++k) {
+                // the stage's activation scales (bulk-copied by the producer)
+                qwait(&bars->xfull[xslot], xph, err, DEV_TIMEOUT_FULL, abort_flag);
+                const float* xst = xring + xslot * (Lay::kXsEntry / 4);
                 for (int gl = 0; gl < gst; ++gl, ++gc) {
                     const int g = k * gst + gl;
-                    const int buf = (int)(gc % kNBuf);
-                    // operands of this group that do not depend on the MMA
-                    float wsv[MULT];
-                    wsv[0] = __ldg(wsrow0 + g);
-                    if (MULT == 2) wsv[MULT - 1] = __ldg(wsrow1 + g);
-                    float xsv[NC];
-                    const float4* xp = reinterpret_cast<const float4*>(a.xs_t + (size_t)g * a.xs_ld + c0);
+                    if ((g >> 2) != qi) {
+                        qi = g >> 2;
 #pragma unroll
-                    for (int j = 0; j < NC / 4; ++j) {
-                        const float4 v = __ldg(xp + j);
-                        xsv[4 * j] = v.x;
-                        xsv[4 * j + 1] = v.y;
-                        xsv[4 * j + 2] = v.z;
-                        xsv[4 * j + 3] = v.w;
+                        for (int m = 0; m < MULT; ++m) {
+                            wcur[m] = wnext[m];
+                            wnext[m] = 4 * qi + 4 < ng ? __ldg(wsq[m] + qi + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        }
                     }
-                    qwait(&bars->tfull[buf], (uint32_t)((gc / kNBuf) & 1), err, DEV_TIMEOUT_TFULL, abort_flag);
-                    __syncwarp();
-                    tc_fence_after();
-                    int d[MULT][NC];
-#pragma unroll
-                    for (int m = 0; m < MULT; ++m)
-                        tmem_ld<NC>(tl + (uint32_t)(buf * N * MULT + m * N + c0), d[m]);
-                    tmem_ld_wait();
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&bars->tempty[buf]);
+                    float wsv[MULT];
 #pragma unroll
                     for (int m = 0; m < MULT; ++m) {
+                        const int e = g & 3;
+                        wsv[m] = e == 0 ? wcur[m].x : e == 1 ? wcur[m].y : e == 2 ? wcur[m].z : wcur[m].w;
+                    }
+                    const float2* xp = reinterpret_cast<const float2*>(xst + gl * N + c0);
+                    qwait(&bars->tfull[buf], bph, err, DEV_TIMEOUT_TFULL, abort_flag);
+                    __syncwarp();
+                    tc_fence_after();
+#pragma unroll
+                    for (int m = 0; m < MULT; ++m) {
+                        // one tensor at a time: its NC dots of this group, then the fp32 update
+                        int d[NC];
+                        tmem_ld<NC>(tl + (uint32_t)(buf * N * MULT + m * N + c0), d);
+                        tmem_ld_wait();
                         const uint64_t w2 = f2_pack(wsv[m], wsv[m]);
 #pragma unroll
                         for (int j = 0; j < NC; j += 2) {
                             // (float)D exactly: the bits of 1.5*2^23 + D, minus 1.5*2^23
-                            const uint64_t df =
-                                f2_add(f2_pack(__int_as_float(d[m][j] + 0x4B400000),
-                                               __int_as_float(d[m][j + 1] + 0x4B400000)),
-                                       f2_pack(-12582912.0f, -12582912.0f));
-                            const uint64_t f = f2_mul(w2, f2_pack(xsv[j], xsv[j + 1]));
+                            const uint64_t df = f2_add(f2_pack(__int_as_float(d[j] + 0x4B400000),
+                                                               __int_as_float(d[j + 1] + 0x4B400000)),
+                                                       f2_pack(-12582912.0f, -12582912.0f));
+                            const float2 xv = xp[j >> 1];
+                            const uint64_t f = f2_mul(w2, f2_pack(xv.x, xv.y));
                             const uint64_t r = f2_fma(f, df, f2_pack(acc[m][j], acc[m][j + 1]));
                             acc[m][j] = f2_lo(r);
                             acc[m][j + 1] = f2_hi(r);
                         }
                     }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bars->tempty[buf]);
+                    if (++buf == kNBuf) {
+                        buf = 0;
+                        bph ^= 1u;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&bars->xempty[xslot]);
+                if (++xslot == kXsStages) {
+                    xslot = 0;
+                    xph ^= 1u;
                 }
             }
             // piece of tile t done: stages [max(s0, tK), send)
@@ -477,8 +575,8 @@ __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_const
             const int P = lastc - first + 1;
             bool finish = true;
             if (P > 1) {
-                const int slot = s0 >= tk0 ? 0 : 1;
-                float* pb = a.part + (((size_t)blockIdx.x * 2 + slot) * MULT) * N * kTileRows;
+                const int pslot0 = s0 >= tk0 ? 0 : 1;
+                float* pb = a.part + (((size_t)blockIdx.x * 2 + pslot0) * MULT) * N * kTileRows;
 #pragma unroll
                 for (int m = 0; m < MULT; ++m)
 #pragma unroll
@@ -515,7 +613,7 @@ __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_const
                 for (int j = 0; j < NC; ++j) {
                     const float v0 = acc[0][j], v1 = __shfl_xor_sync(0xffffffffu, v0, 1);
                     const float u0 = acc[MULT - 1][j], u1 = __shfl_xor_sync(0xffffffffu, u0, 1);
-                    if ((lane & 1) == 0) finish_rows(a.ep, sg, c0 + j, rloc, v0, v1, u0, u1, true);
+                    if ((lane & 1) == 0) finish_pair(a.ep, sg, c0 + j, rloc, v0, v1, u0, u1);
                 }
             }
         }
@@ -523,7 +621,7 @@ __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_const
 
     tc_fence_before();
     __syncthreads();
-    if (warp == 1) {
+    if (warp == kMmaWarp0) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");
     }
@@ -572,7 +670,7 @@ int npad_for(int rows) { return rows <= 16 ? 16 : (rows <= 32 ? 32 : 64); }
 template <int KIND, int N, int MULT>
 cudaError_t launch_t(const QgemmArgs& q, cudaStream_t st, bool pdl, int grid) {
     using Lay = Layout<KIND, N, MULT>;
-    const size_t smem = (size_t)q.stages * Lay::kStage + sizeof(Bars) + 1024;
+    const size_t smem = (size_t)q.stages * Lay::kStage + Lay::kXs + sizeof(Bars) + 1024;
     auto kern = qgemm_kernel<KIND, N, MULT>;
     static size_t set = 0;
     if (smem > set) {
@@ -596,7 +694,7 @@ cudaError_t launch_t(const QgemmArgs& q, cudaStream_t st, bool pdl, int grid) {
 template <int KIND, int N, int MULT>
 int stages_for() {
     using Lay = Layout<KIND, N, MULT>;
-    const int budget = 227 * 1024 - 1024 - (int)sizeof(Bars);
+    const int budget = 227 * 1024 - 1024 - (int)sizeof(Bars) - Lay::kXs;
     int s = budget / Lay::kStage;
     return s > 8 ? 8 : s;
 }
@@ -622,6 +720,7 @@ bool qgemm_ok(const GemvArgs& a, int kind, int rows) {
     if (rows < 1 || rows > 64) return false;
     if (!(a.gs == 32 || a.gs == 64 || a.gs == 128)) return false;
     if (a.cols % kStageK || a.in_mode != IN_QUANT || !a.xq) return false;
+    if ((a.cols / a.gs) % 4) return false;  // weight scales are read four groups at a time
     if (a.nseg < 1 || a.nseg > kMaxSegs) return false;
     for (int i = 0; i < a.nseg; ++i) {
         const GemvSeg& g = a.seg[i];
@@ -657,7 +756,8 @@ cudaError_t qgemm_launch(const GemvArgs& a, int kind, const float* xs_t, int xs_
     const int rows = a.nvalid > 0 ? a.nvalid : a.nb;
     if (!qgemm_ok(a, kind, rows) || !xs_t || !part || !cnt) return cudaErrorInvalidValue;
     const int npad = npad_for(rows);
-    if (xs_ld < npad || xs_ld % 4 || (reinterpret_cast<uintptr_t>(xs_t) & 15u)) return cudaErrorInvalidValue;
+    // the scales of a stage's groups are one contiguous run: row pitch = npad
+    if (xs_ld != npad || (reinterpret_cast<uintptr_t>(xs_t) & 15u)) return cudaErrorInvalidValue;
     QgemmArgs q;
     memset(&q, 0, sizeof(q));
     q.ep = a;
