@@ -198,6 +198,31 @@ float* forward_batch(Transformer* t, const int* tokens, const int* pos, int batc
 /* As forward_batch, writing only the greedy next token of every sequence. */
 int forward_batch_argmax(Transformer* t, const int* tokens, const int* pos, int batch, int* next_tokens);
 
+/* ---- tensor parallelism (the 70B shape over 2, 4 or 8 GPUs) -----------------
+ * The reference runs on one device.  Here one process per GPU holds a
+ * Megatron-style share of every layer: the output rows of wq, wk, wv, w1 and
+ * w3 (its n_heads/tp_size query heads, n_kv_heads/tp_size kv heads and
+ * hidden_dim/tp_size FFN rows) and the matching input columns of wo and w2.
+ * Attention, RoPE, the KV cache and SwiGLU stay local; the wo and w2 products
+ * are partial sums that one NCCL all-reduce per product (two per layer)
+ * completes, inside the captured decode graph.  The embedding, the norms and
+ * the classifier are replicated, so every process returns the full logits.
+ * Every process calls forward / forward_argmax / forward_batch with the same
+ * tokens and positions. */
+
+/* Create the group id (128 bytes) on one process; the caller hands it to the
+ * others (a file, a socket, torch.distributed, ...). */
+int lq_tp_unique_id(void* id128);
+
+/* As build_transformer / build_transformer_random, for process tp_rank of
+ * tp_size (its GPU already selected).  All processes of the group call it;
+ * it returns once every process has joined.  tp_size == 1 needs no id and runs
+ * the tensor-parallel step structure on one GPU. */
+int build_transformer_tp(Transformer** t, const char* checkpoint_path, int max_seq_len, int tp_rank, int tp_size,
+                         const void* id128);
+int build_transformer_random_tp(Transformer** t, const Config* cfg, int kind, int group_size, uint64_t seed,
+                                int max_seq_len, int tp_rank, int tp_size, const void* id128);
+
 /* Release a model (free_transformer, runq.c:285-289). */
 void free_transformer(Transformer* t);
 

@@ -83,6 +83,7 @@ EXPORTS = (
     "lq_synth_tensor", "quantize", "matmul", "matmul_f32", "matmul_f32_noalloc",
     "build_transformer", "build_transformer_random", "forward", "forward_argmax",
     "transformer_reserve_batch", "forward_batch", "forward_batch_argmax",
+    "lq_tp_unique_id", "build_transformer_tp", "build_transformer_random_tp",
     "free_transformer", "transformer_config",
     "lq_write_checkpoint_fp32", "lq_quantize_checkpoint", "lq_read_header", "lq_synth_value",
 )
@@ -123,6 +124,9 @@ def lib() -> C.CDLL:
         "forward": (C.POINTER(F), [P, I, I]),
         "forward_argmax": (I, [P, I, I, C.POINTER(I)]),
         "transformer_reserve_batch": (I, [P, I]),
+        "lq_tp_unique_id": (I, [P]),
+        "build_transformer_tp": (I, [C.POINTER(P), C.c_char_p, I, I, I, P]),
+        "build_transformer_random_tp": (I, [C.POINTER(P), CFG, I, I, U64, I, I, I, P]),
         "forward_batch": (C.POINTER(F), [P, P, P, I]),
         "forward_batch_argmax": (I, [P, P, P, I, P]),
         "free_transformer": (None, [P]),
@@ -249,6 +253,23 @@ class Transformer:
         check(lib().forward_argmax(self._h, token, pos, C.byref(nxt)))
         return nxt.value
 
+    @classmethod
+    def from_file_tp(cls, path: str, rank: int, size: int, group_id: bytes | None, max_seq_len: int = 0):
+        """This process's tensor-parallel share (rank of size) of a checkpoint."""
+        h = C.c_void_p()
+        gid = C.create_string_buffer(group_id, 128) if group_id else None
+        check(lib().build_transformer_tp(C.byref(h), path.encode(), max_seq_len, rank, size, gid))
+        return cls(h.value)
+
+    @classmethod
+    def random_tp(cls, cfg: Config, kind: int, group_size: int, seed: int, rank: int, size: int,
+                  group_id: bytes | None, max_seq_len: int = 0) -> "Transformer":
+        h = C.c_void_p()
+        gid = C.create_string_buffer(group_id, 128) if group_id else None
+        check(lib().build_transformer_random_tp(C.byref(h), C.byref(cfg), kind, group_size, seed, max_seq_len,
+                                                rank, size, gid))
+        return cls(h.value)
+
     def reserve_batch(self, max_batch: int) -> None:
         """Size for up to max_batch sequences (restarts every sequence)."""
         check(lib().transformer_reserve_batch(self._h, max_batch))
@@ -298,6 +319,13 @@ class Transformer:
             self.close()
         except Exception:
             pass
+
+
+def tp_unique_id() -> bytes:
+    """A new tensor-parallel group id (128 bytes) to hand to every process."""
+    buf = C.create_string_buffer(128)
+    check(lib().lq_tp_unique_id(buf))
+    return buf.raw
 
 
 # ---- checkpoint files (host only) ----------------------------------------------

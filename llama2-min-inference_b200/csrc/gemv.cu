@@ -850,7 +850,13 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_cons
         if (blockIdx.x == 0)
             for (int i = ctid; i < n; i += kAqThreads) a.x_out[(size_t)b * n + i] = src[i];
     }
-    const bool norm = a.mode == IN_RMSNORM || a.mode == IN_RMSNORM_EMB;
+    // residual add (tensor-parallel step: y is the all-reduced partial); x_out
+    // is a different buffer from x, so every CTA reads the unmodified x
+    const bool add = a.mode == IN_ADD_RMSNORM;
+    const float* yrow = add ? a.y + (size_t)b * n : nullptr;
+    if (add && blockIdx.x == 0)
+        for (int i = ctid; i < n; i += kAqThreads) a.x_out[(size_t)b * n + i] = src[i] + yrow[i];
+    const bool norm = a.mode == IN_RMSNORM || a.mode == IN_RMSNORM_EMB || add;
     float inv = 1.0f;
     if (norm) {
         // rmsnorm sum of squares: thread t takes float4 chunks t, t+256, ...
@@ -862,6 +868,13 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_cons
             for (int u = 0; u < U; ++u) {
                 const int c = c0 + u * kAqThreads;
                 v[u] = c < n / 4 ? reinterpret_cast<const float4*>(src)[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+                if (add && c < n / 4) {
+                    const float4 w = reinterpret_cast<const float4*>(yrow)[c];
+                    v[u].x += w.x;
+                    v[u].y += w.y;
+                    v[u].z += w.z;
+                    v[u].w += w.w;
+                }
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
@@ -890,6 +903,12 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_cons
         const float4 a1 = *reinterpret_cast<const float4*>(src + k0 + 4);
         v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
         v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+        if (add) {
+            const float4 y0 = *reinterpret_cast<const float4*>(yrow + k0);
+            const float4 y1 = *reinterpret_cast<const float4*>(yrow + k0 + 4);
+            v[0] += y0.x; v[1] += y0.y; v[2] += y0.z; v[3] += y0.w;
+            v[4] += y1.x; v[5] += y1.y; v[6] += y1.z; v[7] += y1.w;
+        }
         if (norm) {
             const float4 w0 = *reinterpret_cast<const float4*>(a.rms_w + k0);
             const float4 w1 = *reinterpret_cast<const float4*>(a.rms_w + k0 + 4);

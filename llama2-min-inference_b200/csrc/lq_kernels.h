@@ -22,6 +22,7 @@ enum InputMode : int {
     IN_F32 = 1,          // fp32 x, quantized in the prologue
     IN_RMSNORM = 2,      // rmsnorm(x) * w, then quantized
     IN_RMSNORM_EMB = 3,  // x = emb[token] (CTA 0 also writes it to x_out), then as IN_RMSNORM
+    IN_ADD_RMSNORM = 4,  // x = x + y (CTA 0 also writes it to x_out), then as IN_RMSNORM (activation quantizer only)
 };
 
 struct GemvSeg {
@@ -97,7 +98,8 @@ cudaError_t qgemm_scales_launch(const float* xs, int rows, int ng, int ld, float
 struct ActQuantArgs {
     int mode;          // IN_F32, IN_RMSNORM or IN_RMSNORM_EMB
     int n, gs, nb;
-    const float* x;    // [nb, n] (IN_F32 / IN_RMSNORM)
+    const float* x;    // [nb, n] (IN_F32 / IN_RMSNORM / IN_ADD_RMSNORM)
+    const float* y;    // [nb, n] IN_ADD_RMSNORM: the (all-reduced) output added to the residual x
     const float* rms_w;
     const float* emb;  // IN_RMSNORM_EMB: x = emb[meta[2b]]
     const int* meta;

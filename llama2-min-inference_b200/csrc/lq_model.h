@@ -41,6 +41,12 @@ struct Transformer {
     int* next = nullptr;                 // [B] argmax
     int* err = nullptr;                  // device error word
     float2* rope = nullptr;              // [max_seq][head_size/2] cos/sin table
+    // tensor parallelism (Megatron split): this process's share of the heads and hidden rows
+    int tp_rank = 0, tp_size = 1;
+    bool tp = false;                     // TP step: partial products, all-reduce, residual add in the quantizer
+    void* comm = nullptr;                // NCCL communicator (tp_size > 1)
+    int nh_l = 0, nkv_l = 0, dq_l = 0, hid_l = 0;  // local query heads, kv heads, q width, hidden rows
+    float *x2 = nullptr, *ybuf = nullptr;  // second residual buffer; all-reduced partial [B][dim]
     // tensor-core GEMM path (steps of mma_min or more sequences)
     int mma_min = 16;
     int xs_ld = 0;                       // max_batch rounded up to 64 (xs_t: a [groups][64] table per 64 rows)

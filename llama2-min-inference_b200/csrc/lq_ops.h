@@ -33,5 +33,9 @@ cudaError_t synth_f32_launch(float* out, int64_t n, uint64_t seed, int tid, floa
                              cudaStream_t st);
 cudaError_t synth_quant_launch(uint8_t* q, float* s, int64_t rows, int64_t cols, int gs, int kind,
                                uint64_t seed, int tid, float std, int64_t row0, cudaStream_t st);
+// columns [col0, col0+cols) of rows [row0, row0+rows) of a tensor with cols_full columns
+cudaError_t synth_quant_cols_launch(uint8_t* q, float* s, int64_t rows, int64_t cols, int64_t cols_full, int64_t col0,
+                                    int gs, int kind, uint64_t seed, int tid, float std, int64_t row0,
+                                    cudaStream_t st);
 
 }  // namespace lq

@@ -15,7 +15,9 @@
 // weight stream starts while its predecessor is finishing.  The graph reads
 // token and position from device memory (the reference's d_meta idea,
 // v5-cuda-fused/run.cu:671-695), so one graph serves every step.
+#include <dlfcn.h>
 #include <fcntl.h>
+#include <nccl.h>  // types only: the library is opened at run time
 #include <sys/mman.h>
 #include <sys/stat.h>
 #include <unistd.h>
@@ -37,6 +39,35 @@ using namespace lq;
 namespace {
 
 int64_t rbytes(int64_t cols, int kind) { return kind == LQ_KIND_INT8 ? cols : cols / 2; }
+
+// NCCL, opened on first use: the copy a host framework already loaded
+// (torch's) when there is one, else the system's libnccl.so.2
+struct Nccl {
+    ncclResult_t (*get_unique_id)(ncclUniqueId*);
+    ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
+    ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*comm_destroy)(ncclComm_t);
+    const char* (*error_string)(ncclResult_t);
+};
+
+const Nccl* nccl() {
+    static Nccl f;
+    static int state = 0;
+    if (state == 0) {
+        void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+        if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        state = -1;
+        if (h) {
+            f.get_unique_id = reinterpret_cast<decltype(f.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
+            f.comm_init_rank = reinterpret_cast<decltype(f.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
+            f.all_reduce = reinterpret_cast<decltype(f.all_reduce)>(dlsym(h, "ncclAllReduce"));
+            f.comm_destroy = reinterpret_cast<decltype(f.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
+            f.error_string = reinterpret_cast<decltype(f.error_string)>(dlsym(h, "ncclGetErrorString"));
+            if (f.get_unique_id && f.comm_init_rank && f.all_reduce && f.comm_destroy && f.error_string) state = 1;
+        }
+    }
+    return state == 1 ? &f : nullptr;
+}
 
 constexpr int kQgTiles = 8192;  // arrival counters: tiles of the largest launch (vocab / 128)
 
@@ -79,12 +110,20 @@ float** f32_by_id(Transformer* t, int id) {
     return nullptr;
 }
 
-int check_config(const Config* c, int gs) {
+int check_config(const Config* c, int gs, int tp_size = 1) {
     LqTensorDesc t[LQ_NT];
     if (lq_tensor_table(c, t) != LQ_OK) return lq_fail(LQ_EINVAL, "bad model config");
     const int hs = c->dim / c->n_heads;
     if (hs % 2 || hs % 4) return lq_fail(LQ_EUNSUPPORTED, "head size %d must be a multiple of 4", hs);
     if (c->dim % gs || c->hidden_dim % gs) return lq_fail(LQ_EINVAL, "dim and hidden_dim must be multiples of gs");
+    if (tp_size > 1) {
+        if (c->n_kv_heads % tp_size || c->n_heads % tp_size)
+            return lq_fail(LQ_EINVAL, "tensor parallelism: %d query / %d kv heads do not split over %d GPUs",
+                           c->n_heads, c->n_kv_heads, tp_size);
+        if ((c->dim / tp_size) % gs || (c->hidden_dim / tp_size) % gs || c->hidden_dim % tp_size)
+            return lq_fail(LQ_EINVAL, "tensor parallelism: dim/%d and hidden_dim/%d must be multiples of gs=%d",
+                           tp_size, tp_size, gs);
+    }
     return LQ_OK;
 }
 
@@ -93,18 +132,26 @@ int alloc_state(Transformer* t) {
     const Config& c = t->c;
     const int B = t->max_batch;
     t->head_size = c.dim / c.n_heads;
-    t->kv_dim = c.dim * c.n_kv_heads / c.n_heads;
     t->kv_mul = c.n_heads / c.n_kv_heads;
+    t->nh_l = c.n_heads / t->tp_size;
+    t->nkv_l = c.n_kv_heads / t->tp_size;
+    t->dq_l = t->nh_l * t->head_size;
+    t->kv_dim = t->nkv_l * t->head_size;  // this process's kv width
+    t->hid_l = c.hidden_dim / t->tp_size;
     t->max_splits = (t->max_seq + kChunk - 1) / kChunk;
     const size_t kv = (size_t)B * c.n_layers * t->kv_dim * t->max_seq;
     int rc = LQ_OK;
     rc = rc ? rc : dalloc(&t->x, (size_t)B * c.dim);
-    rc = rc ? rc : dalloc(&t->q, (size_t)B * c.dim);
-    rc = rc ? rc : dalloc(&t->att, (size_t)B * c.dim);
-    rc = rc ? rc : dalloc(&t->h1, (size_t)B * c.hidden_dim);
-    rc = rc ? rc : dalloc(&t->h3, (size_t)B * c.hidden_dim);
+    rc = rc ? rc : dalloc(&t->q, (size_t)B * t->dq_l);
+    rc = rc ? rc : dalloc(&t->att, (size_t)B * t->dq_l);
+    rc = rc ? rc : dalloc(&t->h1, (size_t)B * t->hid_l);
+    rc = rc ? rc : dalloc(&t->h3, (size_t)B * t->hid_l);
+    if (t->tp) {
+        rc = rc ? rc : dalloc(&t->x2, (size_t)B * c.dim);
+        rc = rc ? rc : dalloc(&t->ybuf, (size_t)B * c.dim);
+    }
     rc = rc ? rc : dalloc(&t->logits, (size_t)B * c.vocab_size);
-    const int maxn = c.hidden_dim > c.dim ? c.hidden_dim : c.dim;
+    const int maxn = t->hid_l > c.dim ? t->hid_l : c.dim;
     // the quantized activation has padding rows up to a multiple of 8: a
     // GEMV launch reads 1, 2, 4 or 8 rows and stores only the valid ones
     const int BP = (B + 7) / 8 * 8;
@@ -113,8 +160,8 @@ int alloc_state(Transformer* t) {
     rc = rc ? rc : dalloc(&t->xqsum, (size_t)BP * (maxn / t->gs));
     rc = rc ? rc : dalloc(&t->kc, kv);
     rc = rc ? rc : dalloc(&t->vc, kv);
-    rc = rc ? rc : dalloc(&t->part, (size_t)B * c.n_heads * t->max_splits * (t->head_size + 2));
-    rc = rc ? rc : dalloc(&t->counters, (size_t)B * c.n_kv_heads);
+    rc = rc ? rc : dalloc(&t->part, (size_t)B * t->nh_l * t->max_splits * (t->head_size + 2));
+    rc = rc ? rc : dalloc(&t->counters, (size_t)B * t->nkv_l);
     rc = rc ? rc : dalloc(&t->meta, (size_t)2 * B);
     rc = rc ? rc : dalloc(&t->next, (size_t)B);
     rc = rc ? rc : dalloc(&t->err, 1);
@@ -137,7 +184,7 @@ int alloc_state(Transformer* t) {
         cudaError_t e0 = cudaMemcpy(t->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice);
         if (e0 != cudaSuccess) return cuda_fail(e0, "rope table");
     }
-    cudaError_t e = cudaMemset(t->counters, 0, (size_t)B * c.n_kv_heads * sizeof(int));
+    cudaError_t e = cudaMemset(t->counters, 0, (size_t)B * t->nkv_l * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(t->qg_cnt, 0, (size_t)kQgTiles * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(t->xs_t, 0, (size_t)t->xs_ld * (maxn / t->gs) * sizeof(float));
     if (e == cudaSuccess) e = cudaMemset(t->xq, 0, (size_t)BP * maxn);
@@ -167,9 +214,10 @@ void free_state(Transformer* t) {
     t->graph = nullptr;
     t->graph_batch = 0;
     void* bufs[] = {t->x, t->q, t->att, t->h1, t->h3, t->xq, t->xqs, t->xqsum, t->logits, t->kc, t->vc,
-                    t->part, t->counters, t->meta, t->next, t->err, t->rope, t->xs_t, t->qg_part, t->qg_cnt};
+                    t->part, t->counters, t->meta, t->next, t->err, t->rope, t->xs_t, t->qg_part, t->qg_cnt,
+                    t->x2, t->ybuf};
     for (void* b : bufs) cudaFree(b);
-    t->xs_t = t->qg_part = nullptr;
+    t->xs_t = t->qg_part = t->x2 = t->ybuf = nullptr;
     t->qg_cnt = nullptr;
     t->x = t->q = t->att = t->h1 = t->h3 = t->logits = t->kc = t->vc = t->part = nullptr;
     t->xq = nullptr;
@@ -273,10 +321,11 @@ namespace lq {
 int forward_launch(Transformer* t, int batch) {
     const Config& c = t->c;
     const int kind = t->kind, gs = t->gs;
-    const int D = c.dim, H = c.hidden_dim, KV = t->kv_dim, hs = t->head_size;
-    const int64_t rbD = rbytes(D, kind), rbH = rbytes(H, kind);
-    const int ngD = D / gs, ngH = H / gs;
-    const int64_t kv_layer = (int64_t)c.n_kv_heads * t->max_seq * hs;
+    // local widths: the whole model on one GPU, or this process's share under tensor parallelism
+    const int D = c.dim, DQ = t->dq_l, H = t->hid_l, KV = t->kv_dim, hs = t->head_size;
+    const int64_t rbD = rbytes(D, kind), rbQ = rbytes(DQ, kind), rbH = rbytes(H, kind);
+    const int ngD = D / gs, ngQ = DQ / gs, ngH = H / gs;
+    const int64_t kv_layer = (int64_t)t->nkv_l * t->max_seq * hs;
     const int64_t kv_seq = (int64_t)c.n_layers * kv_layer;
     cudaStream_t st = t->stream;
     auto base = [&](GemvArgs& a, int cols) {
@@ -294,17 +343,19 @@ int forward_launch(Transformer* t, int batch) {
     };
     cudaError_t e;
     // activation quantizer in front of every GEMV (quantize_act, runq.c:345,394,400,412,418)
-    auto quant = [&](int mode, const float* x, int n, const float* rms_w) -> cudaError_t {
+    auto quant = [&](int mode, const float* x, int n, const float* rms_w, float* x_out = nullptr,
+                     const float* y = nullptr) -> cudaError_t {
         ActQuantArgs q{};
         q.mode = mode;
         q.n = n;
         q.gs = gs;
         q.nb = batch;
         q.x = x;
+        q.y = y;
         q.rms_w = rms_w;
         q.emb = t->emb;
         q.meta = t->meta;
-        q.x_out = t->x;
+        q.x_out = x_out ? x_out : t->x;
         q.xq = t->xq;
         q.xs = t->xqs;
         q.xsum = t->xqsum;
@@ -322,21 +373,40 @@ int forward_launch(Transformer* t, int batch) {
         a.xs = t->xqs;
         a.xsum_in = t->xqsum;
     };
+    // tensor parallelism: wo and w2 give partial sums over this process's
+    // columns; they are all-reduced and added to the residual stream by the
+    // next quantizer, which reads one residual buffer and writes the other
+    auto allreduce = [&]() -> int {
+        if (t->tp_size == 1) return LQ_OK;
+        const ncclResult_t r = nccl()->all_reduce(t->ybuf, t->ybuf, (size_t)batch * D, ncclFloat, ncclSum,
+                                                  static_cast<ncclComm_t>(t->comm), st);
+        return r == ncclSuccess ? LQ_OK : lq_fail(LQ_ECUDA, "all-reduce: %s", nccl()->error_string(r));
+    };
+    float* xa = t->x;              // residual stream after attention's add (and the embedding)
+    float* xb = t->tp ? t->x2 : t->x;  // after the ffn's add
+    int rc;
     for (int l = 0; l < c.n_layers; ++l) {
         GemvArgs a;
         // 1. q, k, v (attention rmsnorm + quantize first; layer 0 starts from emb[token])
-        if ((e = quant(l == 0 ? IN_RMSNORM_EMB : IN_RMSNORM, t->x, D, t->rms_att + (size_t)l * D)) != cudaSuccess)
-            return cuda_fail(e, "attention rmsnorm");
+        const float* rms_a = t->rms_att + (size_t)l * D;
+        if (l == 0)
+            e = quant(IN_RMSNORM_EMB, xa, D, rms_a, xa);
+        else if (t->tp)
+            e = quant(IN_ADD_RMSNORM, xb, D, rms_a, xa, t->ybuf);
+        else
+            e = quant(IN_RMSNORM, xa, D, rms_a);
+        if (e != cudaSuccess) return cuda_fail(e, "attention rmsnorm");
         base(a, D);
-        a.seg[0] = {t->wq.q + (size_t)l * D * rbD, t->wq.s + (size_t)l * D * ngD, t->q, D, EPI_ROPE_Q};
+        a.seg[0] = {t->wq.q + (size_t)l * DQ * rbD, t->wq.s + (size_t)l * DQ * ngD, t->q, DQ, EPI_ROPE_Q};
         a.seg[1] = {t->wk.q + (size_t)l * KV * rbD, t->wk.s + (size_t)l * KV * ngD, nullptr, KV, EPI_ROPE_KCACHE};
         a.seg[2] = {t->wv.q + (size_t)l * KV * rbD, t->wv.s + (size_t)l * KV * ngD, nullptr, KV, EPI_VCACHE};
         a.nseg = 3;
+        a.y_stride = DQ;
         qin(a);
         a.kcache = t->kc + l * kv_layer;
         a.vcache = t->vc + l * kv_layer;
         if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
-        // 2. attention
+        // 2. attention (this process's heads)
         AttnArgs at{};
         at.q = t->q;
         at.kcache = t->kc + l * kv_layer;
@@ -347,24 +417,27 @@ int forward_launch(Transformer* t, int batch) {
         at.meta = t->meta;
         at.err = t->err;
         at.kv_seq_stride = kv_seq;
-        at.q_stride = D;
-        at.n_heads = c.n_heads;
-        at.n_kv_heads = c.n_kv_heads;
+        at.q_stride = DQ;
+        at.n_heads = t->nh_l;
+        at.n_kv_heads = t->nkv_l;
         at.kv_mul = t->kv_mul;
         at.head_size = hs;
         at.max_seq = t->max_seq;
         at.max_splits = t->max_splits;
         if ((e = attention_launch(at, batch, st, true)) != cudaSuccess) return cuda_fail(e, "attention");
         // 3. wo + residual
-        if ((e = quant(IN_F32, t->att, D, nullptr)) != cudaSuccess) return cuda_fail(e, "attention output quantize");
-        base(a, D);
-        a.seg[0] = {t->wo.q + (size_t)l * D * rbD, t->wo.s + (size_t)l * D * ngD, t->x, D, EPI_ADD};
+        if ((e = quant(IN_F32, t->att, DQ, nullptr)) != cudaSuccess) return cuda_fail(e, "attention output quantize");
+        base(a, DQ);
+        a.seg[0] = {t->wo.q + (size_t)l * D * rbQ, t->wo.s + (size_t)l * D * ngQ, t->tp ? t->ybuf : xa, D,
+                    t->tp ? EPI_STORE : EPI_ADD};
         a.nseg = 1;
         qin(a);
         if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "wo gemv");
+        if ((rc = allreduce())) return rc;
         // 4. w1 | w3 paired, SwiGLU in the epilogue: h1 = silu(x.w1) * (x.w3)
-        if ((e = quant(IN_RMSNORM, t->x, D, t->rms_ffn + (size_t)l * D)) != cudaSuccess)
-            return cuda_fail(e, "ffn rmsnorm");
+        const float* rms_f = t->rms_ffn + (size_t)l * D;
+        e = t->tp ? quant(IN_ADD_RMSNORM, xa, D, rms_f, xb, t->ybuf) : quant(IN_RMSNORM, xa, D, rms_f);
+        if (e != cudaSuccess) return cuda_fail(e, "ffn rmsnorm");
         base(a, D);
         a.seg[0] = {t->w1.q + (size_t)l * H * rbD, t->w1.s + (size_t)l * H * ngD, t->h1, H, EPI_SWIGLU,
                     t->w3.q + (size_t)l * H * rbD, t->w3.s + (size_t)l * H * ngD};
@@ -376,13 +449,16 @@ int forward_launch(Transformer* t, int batch) {
         // 5. w2 + residual
         if ((e = quant(IN_F32, t->h1, H, nullptr)) != cudaSuccess) return cuda_fail(e, "ffn quantize");
         base(a, H);
-        a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->x, D, EPI_ADD};
+        a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->tp ? t->ybuf : xb, D,
+                    t->tp ? EPI_STORE : EPI_ADD};
         a.nseg = 1;
         qin(a);
         if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
+        if ((rc = allreduce())) return rc;
     }
     GemvArgs a;
-    if ((e = quant(IN_RMSNORM, t->x, D, t->rms_final)) != cudaSuccess) return cuda_fail(e, "final rmsnorm");
+    e = t->tp ? quant(IN_ADD_RMSNORM, xb, D, t->rms_final, xa, t->ybuf) : quant(IN_RMSNORM, xa, D, t->rms_final);
+    if (e != cudaSuccess) return cuda_fail(e, "final rmsnorm");
     base(a, D);
     a.seg[0] = {t->wcls.q, t->wcls.s, t->logits, c.vocab_size, EPI_STORE};
     a.nseg = 1;
@@ -469,25 +545,133 @@ int run_step(Transformer* t, const int* tokens, const int* pos, int batch, bool 
 
 }  // namespace lq
 
-extern "C" {
+namespace {
 
-int build_transformer(Transformer** out, const char* path, int max_seq_len) {
+// How tensor parallelism splits a stacked [L * rows, cols] tensor: 0 = whole
+// (embedding-side and classifier tensors, replicated), 1 = output rows of
+// every layer (wq, wk, wv, w1, w3), 2 = input columns (wo, w2).
+int tp_split(int id) {
+    switch (id) {
+        case LQ_T_WQ: case LQ_T_WK: case LQ_T_WV: case LQ_T_W1: case LQ_T_W3: return 1;
+        case LQ_T_WO: case LQ_T_W2: return 2;
+    }
+    return 0;
+}
+
+// this process's rows x cols of tensor d
+void tp_local_shape(const Transformer* t, const LqTensorDesc& d, int64_t* rows, int64_t* cols) {
+    *rows = d.rows;
+    *cols = d.cols;
+    if (!t->tp) return;
+    if (tp_split(d.id) == 1) *rows = d.rows / t->tp_size;
+    if (tp_split(d.id) == 2) *cols = d.cols / t->tp_size;
+}
+
+int tp_join(Transformer* t, int rank, int size, const void* id) {
+    t->tp = true;
+    t->tp_rank = rank;
+    t->tp_size = size;
+    if (size == 1) return LQ_OK;
+    const Nccl* f = nccl();
+    if (!f) return lq_fail(LQ_EUNSUPPORTED, "tensor parallelism needs NCCL (libnccl.so.2), which could not be loaded");
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof(uid));
+    ncclComm_t comm = nullptr;
+    const ncclResult_t r = f->comm_init_rank(&comm, size, uid, rank);
+    if (r != ncclSuccess) return lq_fail(LQ_ECUDA, "NCCL communicator (rank %d of %d): %s", rank, size, f->error_string(r));
+    t->comm = comm;
+    return LQ_OK;
+}
+
+// Read the checkpoint's tensors (mmap'd at data + hb) into t, this process's
+// share of each under tensor parallelism.
+int upload_weights(Transformer* t, const uint8_t* data, size_t hb, int shared) {
+    const Config& c = t->c;
+    const int kind = t->kind, gs = t->gs, L = c.n_layers;
+    LqTensorDesc td[LQ_NT];
+    lq_tensor_table(&c, td);
+    const uint8_t* p = data + hb;
+    int rc = LQ_OK;
+    for (int i = 0; i < LQ_NT && !rc; ++i) {
+        const LqTensorDesc& d = td[i];
+        cudaError_t e = cudaSuccess;
+        if (d.id == LQ_T_WCLS && shared) {
+            // extension: quantize the fp32 embedding as the classifier
+            rc = alloc_q(t->wcls, d.rows, d.cols, gs, kind);
+            if (rc) break;
+            std::vector<uint8_t> q((size_t)(d.rows * rbytes(d.cols, kind)));
+            std::vector<float> sc((size_t)(d.rows * (d.cols / gs)));
+            std::vector<float> emb((size_t)(d.rows * d.cols));
+            cudaMemcpy(emb.data(), t->emb, emb.size() * 4, cudaMemcpyDeviceToHost);
+            lq_quantize_rows_host(emb.data(), d.rows, d.cols, gs, kind, q.data(), sc.data());
+            e = cudaMemcpy(t->wcls.q, q.data(), q.size(), cudaMemcpyHostToDevice);
+            if (e == cudaSuccess) e = cudaMemcpy(t->wcls.s, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice);
+        } else if (d.quantized) {
+            QW* w = weight_by_id(t, d.id);
+            int64_t rows, cols;
+            tp_local_shape(t, d, &rows, &cols);
+            rc = alloc_q(*w, rows, cols, gs, kind);
+            if (rc) break;
+            const size_t rbf = (size_t)rbytes(d.cols, kind), ngf = (size_t)(d.cols / gs);
+            const size_t qb = (size_t)d.rows * rbf, sb = (size_t)d.rows * ngf * 4;
+            const int split = t->tp ? tp_split(d.id) : 0;
+            if (split == 0) {
+                e = cudaMemcpy(w->q, p, qb, cudaMemcpyHostToDevice);
+                if (e == cudaSuccess) e = cudaMemcpy(w->s, p + qb, sb, cudaMemcpyHostToDevice);
+            } else {
+                const int64_t rl = d.rows / L;  // rows of one layer
+                for (int l = 0; l < L && e == cudaSuccess; ++l) {
+                    if (split == 1) {
+                        // this process's rows of layer l
+                        const int64_t r0 = l * rl + t->tp_rank * (rl / t->tp_size), nr = rl / t->tp_size;
+                        e = cudaMemcpy(w->q + (size_t)l * nr * rbf, p + (size_t)r0 * rbf, (size_t)nr * rbf,
+                                       cudaMemcpyHostToDevice);
+                        if (e == cudaSuccess)
+                            e = cudaMemcpy(w->s + (size_t)l * nr * ngf, p + qb + (size_t)r0 * ngf * 4, (size_t)nr * ngf * 4,
+                                           cudaMemcpyHostToDevice);
+                    } else {
+                        // this process's columns of every row of layer l (whole groups)
+                        const size_t rbl = (size_t)rbytes(cols, kind), ngl = (size_t)(cols / gs);
+                        const size_t c0b = (size_t)rbytes(t->tp_rank * cols, kind), c0g = (size_t)(t->tp_rank * cols / gs);
+                        e = cudaMemcpy2D(w->q + (size_t)l * rl * rbl, rbl, p + (size_t)l * rl * rbf + c0b, rbf, rbl,
+                                         (size_t)rl, cudaMemcpyHostToDevice);
+                        if (e == cudaSuccess)
+                            e = cudaMemcpy2D(w->s + (size_t)l * rl * ngl, ngl * 4, p + qb + ((size_t)l * rl * ngf + c0g) * 4,
+                                             ngf * 4, ngl * 4, (size_t)rl, cudaMemcpyHostToDevice);
+                    }
+                }
+            }
+            p += qb + sb;
+        } else {
+            float** f = f32_by_id(t, d.id);
+            const size_t n = (size_t)(d.rows * d.cols);
+            rc = dalloc(f, n);
+            if (rc) break;
+            e = cudaMemcpy(*f, p, n * 4, cudaMemcpyHostToDevice);
+            p += n * 4;
+        }
+        if (!rc && e != cudaSuccess) rc = cuda_fail(e, "weight upload");
+    }
+    return rc;
+}
+
+int build_file(Transformer** out, const char* path, int max_seq_len, bool tp, int rank, int size, const void* id) {
     if (!out || !path) return lq_fail(LQ_EINVAL, "build_transformer: null argument");
     *out = nullptr;
     int fd = open(path, O_RDONLY);
     if (fd < 0) return lq_fail(LQ_EIO, "couldn't open file %s", path);
     struct stat st;
     fstat(fd, &st);
-    const size_t size = (size_t)st.st_size;
-    const uint8_t* data = size ? (const uint8_t*)mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0)
-                               : (const uint8_t*)MAP_FAILED;
+    const size_t size_b = (size_t)st.st_size;
+    const uint8_t* data = size_b ? (const uint8_t*)mmap(nullptr, size_b, PROT_READ, MAP_PRIVATE, fd, 0)
+                                 : (const uint8_t*)MAP_FAILED;
     close(fd);
     if (data == MAP_FAILED) return lq_fail(LQ_EIO, "mmap failed: %s", path);
     Config c;
     int kind, gs, shared;
     size_t hb;
-    int rc = lq_parse_header(data, size, &c, &kind, &gs, &shared, &hb);
-    if (!rc) rc = check_config(&c, gs);
+    int rc = lq_parse_header(data, size_b, &c, &kind, &gs, &shared, &hb);
+    if (!rc) rc = check_config(&c, gs, tp ? size : 1);
     LqTensorDesc td[LQ_NT];
     if (!rc) rc = lq_tensor_table(&c, td);
     // size check (the reference does none: runq.c:269-277)
@@ -498,48 +682,17 @@ int build_transformer(Transformer** out, const char* path, int max_seq_len) {
             need += td[i].quantized ? (size_t)lq_qtensor_bytes(td[i].rows, td[i].cols, gs, kind)
                                     : (size_t)(td[i].rows * td[i].cols * 4);
         }
-        if (need > size) rc = lq_fail(LQ_EFORMAT, "truncated checkpoint: %zu bytes, need %zu", size, need);
+        if (need > size_b) rc = lq_fail(LQ_EFORMAT, "truncated checkpoint: %zu bytes, need %zu", size_b, need);
     }
     Transformer* t = nullptr;
     if (!rc) {
         t = new_transformer(&c, kind, gs, max_seq_len, 1);
         t->shared = shared;
-        const uint8_t* p = data + hb;
-        for (int i = 0; i < LQ_NT && !rc; ++i) {
-            const LqTensorDesc& d = td[i];
-            cudaError_t e = cudaSuccess;
-            if (d.id == LQ_T_WCLS && shared) {
-                // extension: quantize the fp32 embedding as the classifier
-                rc = alloc_q(t->wcls, d.rows, d.cols, gs, kind);
-                if (rc) break;
-                std::vector<uint8_t> q((size_t)(d.rows * rbytes(d.cols, kind)));
-                std::vector<float> s((size_t)(d.rows * (d.cols / gs)));
-                std::vector<float> emb((size_t)(d.rows * d.cols));
-                cudaMemcpy(emb.data(), t->emb, emb.size() * 4, cudaMemcpyDeviceToHost);
-                lq_quantize_rows_host(emb.data(), d.rows, d.cols, gs, kind, q.data(), s.data());
-                e = cudaMemcpy(t->wcls.q, q.data(), q.size(), cudaMemcpyHostToDevice);
-                if (e == cudaSuccess) e = cudaMemcpy(t->wcls.s, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
-            } else if (d.quantized) {
-                QW* w = weight_by_id(t, d.id);
-                rc = alloc_q(*w, d.rows, d.cols, gs, kind);
-                if (rc) break;
-                const size_t qb = (size_t)(d.rows * rbytes(d.cols, kind)), sb = (size_t)(d.rows * (d.cols / gs) * 4);
-                e = cudaMemcpy(w->q, p, qb, cudaMemcpyHostToDevice);
-                if (e == cudaSuccess) e = cudaMemcpy(w->s, p + qb, sb, cudaMemcpyHostToDevice);
-                p += qb + sb;
-            } else {
-                float** f = f32_by_id(t, d.id);
-                const size_t n = (size_t)(d.rows * d.cols);
-                rc = dalloc(f, n);
-                if (rc) break;
-                e = cudaMemcpy(*f, p, n * 4, cudaMemcpyHostToDevice);
-                p += n * 4;
-            }
-            if (!rc && e != cudaSuccess) rc = cuda_fail(e, "weight upload");
-        }
+        if (tp) rc = tp_join(t, rank, size, id);
+        if (!rc) rc = upload_weights(t, data, hb, shared);
         if (!rc) rc = alloc_state(t);
     }
-    munmap((void*)data, size);
+    munmap((void*)data, size_b);
     if (rc) {
         if (t) free_transformer(t);
         return rc;
@@ -548,26 +701,47 @@ int build_transformer(Transformer** out, const char* path, int max_seq_len) {
     return LQ_OK;
 }
 
-int build_transformer_random(Transformer** out, const Config* cfg, int kind, int gs, uint64_t seed,
-                             int max_seq_len) {
+int build_random(Transformer** out, const Config* cfg, int kind, int gs, uint64_t seed, int max_seq_len, bool tp,
+                 int rank, int size, const void* id) {
     if (!out || !cfg) return lq_fail(LQ_EINVAL, "build_transformer_random: null argument");
     *out = nullptr;
     if (kind != LQ_KIND_INT8 && kind != LQ_KIND_INT4) return lq_fail(LQ_EINVAL, "kind must be INT8 or INT4");
     if (!(gs == 32 || gs == 64 || gs == 128 || gs == 256)) return lq_fail(LQ_EUNSUPPORTED, "group size %d", gs);
-    int rc = check_config(cfg, gs);
+    int rc = check_config(cfg, gs, tp ? size : 1);
     if (rc) return rc;
     LqTensorDesc td[LQ_NT];
     lq_tensor_table(cfg, td);
     Transformer* t = new_transformer(cfg, kind, gs, max_seq_len, 1);
+    if (tp) rc = tp_join(t, rank, size, id);
     const float std = 0.02f;
+    const int L = cfg->n_layers;
     for (int i = 0; i < LQ_NT && !rc; ++i) {
         const LqTensorDesc& d = td[i];
-        cudaError_t e;
+        cudaError_t e = cudaSuccess;
         if (d.quantized) {
             QW* w = weight_by_id(t, d.id);
-            rc = alloc_q(*w, d.rows, d.cols, gs, kind);
+            int64_t rows, cols;
+            tp_local_shape(t, d, &rows, &cols);
+            rc = alloc_q(*w, rows, cols, gs, kind);
             if (rc) break;
-            e = synth_quant_launch(w->q, w->s, d.rows, d.cols, gs, kind, seed, d.id, std, 0, nullptr);
+            const int split = t->tp ? tp_split(d.id) : 0;
+            if (split == 0) {
+                e = synth_quant_launch(w->q, w->s, d.rows, d.cols, gs, kind, seed, d.id, std, 0, nullptr);
+            } else {
+                // the generator is indexed by (row, column) of the whole tensor: each
+                // process generates exactly its share of the unsplit model's weights
+                const int64_t rl = d.rows / L, nr = rows / L;
+                const size_t rbl = (size_t)rbytes(cols, kind), ngl = (size_t)(cols / gs);
+                for (int l = 0; l < L && e == cudaSuccess; ++l) {
+                    if (split == 1)
+                        e = synth_quant_launch(w->q + (size_t)l * nr * rbl, w->s + (size_t)l * nr * ngl, nr, cols, gs, kind,
+                                               seed, d.id, std, l * rl + t->tp_rank * nr, nullptr);
+                    else
+                        e = synth_quant_cols_launch(w->q + (size_t)l * rl * rbl, w->s + (size_t)l * rl * ngl, rl, cols,
+                                                    d.cols, t->tp_rank * cols, gs, kind, seed, d.id, std, l * rl,
+                                                    nullptr);
+                }
+            }
         } else {
             float** f = f32_by_id(t, d.id);
             const int64_t n = d.rows * d.cols;
@@ -591,6 +765,48 @@ int build_transformer_random(Transformer** out, const Config* cfg, int kind, int
     return LQ_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+int build_transformer(Transformer** out, const char* path, int max_seq_len) {
+    return build_file(out, path, max_seq_len, false, 0, 1, nullptr);
+}
+
+int build_transformer_random(Transformer** out, const Config* cfg, int kind, int gs, uint64_t seed,
+                             int max_seq_len) {
+    return build_random(out, cfg, kind, gs, seed, max_seq_len, false, 0, 1, nullptr);
+}
+
+int lq_tp_unique_id(void* id) {
+    if (!id) return lq_fail(LQ_EINVAL, "lq_tp_unique_id: null argument");
+    const Nccl* f = nccl();
+    if (!f) return lq_fail(LQ_EUNSUPPORTED, "tensor parallelism needs NCCL (libnccl.so.2), which could not be loaded");
+    ncclUniqueId uid;
+    const ncclResult_t r = f->get_unique_id(&uid);
+    if (r != ncclSuccess) return lq_fail(LQ_ECUDA, "ncclGetUniqueId: %s", f->error_string(r));
+    memcpy(id, &uid, sizeof(uid));
+    return LQ_OK;
+}
+
+static int tp_args_ok(int rank, int size, const void* id) {
+    if (size < 1 || size > 64 || rank < 0 || rank >= size) return lq_fail(LQ_EINVAL, "tp rank %d of %d", rank, size);
+    if (size > 1 && !id) return lq_fail(LQ_EINVAL, "tensor parallelism over %d GPUs needs the group id", size);
+    return LQ_OK;
+}
+
+int build_transformer_tp(Transformer** out, const char* path, int max_seq_len, int tp_rank, int tp_size,
+                         const void* id) {
+    int rc = tp_args_ok(tp_rank, tp_size, id);
+    return rc ? rc : build_file(out, path, max_seq_len, true, tp_rank, tp_size, id);
+}
+
+int build_transformer_random_tp(Transformer** out, const Config* cfg, int kind, int gs, uint64_t seed,
+                                int max_seq_len, int tp_rank, int tp_size, const void* id) {
+    int rc = tp_args_ok(tp_rank, tp_size, id);
+    return rc ? rc : build_random(out, cfg, kind, gs, seed, max_seq_len, true, tp_rank, tp_size, id);
+}
+
 float* forward(Transformer* t, int token, int pos) {
     if (!t) {
         lq_fail(LQ_EINVAL, "forward: null transformer");
@@ -610,7 +826,9 @@ int forward_argmax(Transformer* t, int token, int pos, int* next_token) {
 
 void free_transformer(Transformer* t) {
     if (!t) return;
-    free_state(t);
+    free_state(t);  // the captured graph (which holds the all-reduces) goes before the communicator
+    if (t->comm && nccl()) nccl()->comm_destroy(static_cast<ncclComm_t>(t->comm));
+    t->comm = nullptr;
     QW* ws[] = {&t->wq, &t->wk, &t->wv, &t->wo, &t->w1, &t->w2, &t->w3, &t->wcls};
     for (QW* w : ws) {
         cudaFree(w->q);

@@ -300,16 +300,18 @@ __global__ void synth_f32_kernel(float* out, int64_t n, uint64_t seedmix, int ti
         out[i] = ones ? 1.0f : synth(seedmix, tid, (uint64_t)i, scale);
 }
 
-// one thread per group: weights of rows [row0, row0+rows) of tensor `tid`
+// one thread per group: weights of rows [row0, row0+rows), columns
+// [col0, col0+cols) of tensor `tid` whose rows hold cols_full values
 __global__ void synth_quant_kernel(uint8_t* q, float* s, int64_t rows, int64_t cols, int gs, int kind,
-                                   uint64_t seedmix, int tid, float scale, int64_t row0) {
+                                   uint64_t seedmix, int tid, float scale, int64_t row0, int64_t cols_full,
+                                   int64_t col0) {
     const int64_t ng = cols / gs;
     const int64_t total = rows * ng;
     float v[256];
     for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
          t += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = t / ng, g = t - r * ng;
-        const uint64_t e0 = (uint64_t)(row0 + r) * cols + g * gs;
+        const uint64_t e0 = (uint64_t)(row0 + r) * cols_full + col0 + g * gs;
         float amax = 0.0f;
         for (int j = 0; j < gs; ++j) {
             v[j] = synth(seedmix, tid, e0 + j, scale);
@@ -360,7 +362,19 @@ cudaError_t synth_quant_launch(uint8_t* q, float* s, int64_t rows, int64_t cols,
     int64_t blocks = (groups + 127) / 128;
     if (blocks > 65536) blocks = 65536;
     synth_quant_kernel<<<(unsigned)blocks, 128, 0, st>>>(q, s, rows, cols, gs, kind, host_mix64(seed), tid,
-                                                          scale, row0);
+                                                          scale, row0, cols, 0);
+    return cudaGetLastError();
+}
+
+cudaError_t synth_quant_cols_launch(uint8_t* q, float* s, int64_t rows, int64_t cols, int64_t cols_full, int64_t col0,
+                                    int gs, int kind, uint64_t seed, int tid, float std, int64_t row0,
+                                    cudaStream_t st) {
+    const float scale = std * 5.9604644775390625e-8f;
+    const int64_t groups = rows * (cols / gs);
+    int64_t blocks = (groups + 127) / 128;
+    if (blocks > 65536) blocks = 65536;
+    synth_quant_kernel<<<(unsigned)blocks, 128, 0, st>>>(q, s, rows, cols, gs, kind, host_mix64(seed), tid,
+                                                          scale, row0, cols_full, col0);
     return cudaGetLastError();
 }
 
