@@ -348,6 +348,25 @@ def tp_bench(lq, torch, rank, world, dist, ctx: int = 2048, steps1: int = 16, st
             "init_s": round(init_s, 1), "runs": runs}
 
 
+def probe(spec: str):
+    """One small decode case for profilers: "LAYERS:BATCH:KIND:CTX" on the
+    Llama-2-13B layer shape (3 warm steps, 1 timed step, printed in ms)."""
+    import torch
+
+    L, B, kind, ctx = (int(v) for v in spec.split(":"))
+    lq = importlib.import_module("llama2-min-inference_b200")
+    t = lq.Transformer.random(lq.Config.make(5120, 13824, L, 40, 40, 32000, 4096), kind, 64, 11, ctx + 16)
+    t.reserve_batch(B)
+    tok = np.ones(B, np.int32)
+    for w in range(3):
+        tok = t.forward_batch_argmax(tok, np.full(B, ctx - 3 + w, np.int32))
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    t.forward_batch_argmax(tok, np.full(B, ctx, np.int32))
+    print(f"probe {spec}: {1e3 * (time.perf_counter() - t0):.3f} ms", flush=True)
+    t.close()
+
+
 def run_gpu(args):
     import torch
 
@@ -507,10 +526,13 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-batch", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
+    ap.add_argument("--probe", default=None, help="LAYERS:BATCH:KIND:CTX: one small 13B-shape step for profilers")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.probe:
+        probe(args.probe)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)
