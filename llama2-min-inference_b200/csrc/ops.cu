@@ -104,16 +104,36 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         return;
     }
 
-    // scores: warp per position, lanes over dims
+    // scores: warp per position, lanes over dims.  Four positions at a time per
+    // warp: independent dot products and reductions interleave (each one in
+    // the same order as alone).
     const float rs = sqrtf((float)hs);
-    for (int t = warp; t < nt; t += NW) {
-        const float* kt = ks + t * hs;
+    constexpr int U = 4;
+    for (int t0w = warp; t0w < nt; t0w += U * NW) {
         for (int j = 0; j < km; ++j) {
             const float* qj = qs + j * hs;
-            float p = 0.0f;
-            for (int i = lane; i < hs; i += 32) p = fmaf(qj[i], kt[i], p);
-            p = warp_sum(p);
-            if (lane == 0) sc[j * kChunk + t] = p / rs;
+            float p[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) p[u] = 0.0f;
+#pragma unroll 4
+            for (int i = lane; i < hs; i += 32) {
+                const float qv = qj[i];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int t = t0w + u * NW;
+                    if (t < nt) p[u] = fmaf(qv, ks[t * hs + i], p[u]);
+                }
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+                for (int u = 0; u < U; ++u) p[u] += __shfl_xor_sync(0xffffffffu, p[u], o);
+            if (lane == 0)
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int t = t0w + u * NW;
+                    if (t < nt) sc[j * kChunk + t] = p[u] / rs;
+                }
         }
     }
     __syncthreads();
@@ -142,6 +162,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         const int j = i / hs, d = i - j * hs;
         const float* pj = sc + j * kChunk;
         float o = 0.0f;
+#pragma unroll 8
         for (int t = 0; t < nt; ++t) o = fmaf(pj[t], vs[t * hs + d], o);
         if (nsplit == 1) {
             out[i] = o / ml[2 * j + 1];
@@ -171,8 +192,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         const int j = i / hs, d = i - j * hs;
         const float* base = a.part + (((size_t)b * a.n_heads + hq0 + j) * a.max_splits) * (hs + 2);
         float M = -FLT_MAX;
+#pragma unroll 8
         for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(base + (size_t)s * (hs + 2)));
         float L = 0.0f, o = 0.0f;
+#pragma unroll 4
         for (int s = 0; s < nsplit; ++s) {
             const float* ps = base + (size_t)s * (hs + 2);
             const float w = lq_expf(__ldcg(ps) - M);
