@@ -298,54 +298,73 @@ def batch_bench(lq, torch, batches=(1, 8, 16, 32, 64), ctx: int = 1024, steps: i
 
 def tp_bench(lq, torch, rank, world, dist, ctx: int = 2048, steps1: int = 16, steps16: int = 8):
     """Config 5: Llama-2-70B-shape INT4 GS64 decode, tensor-parallel over the
-    job's GPUs (one process per GPU, NCCL all-reduce after wo and w2),
-    batch 1 and batch 16 at context ctx (cache positions below ctx
-    zero-filled, not decoded).  Every process runs the same steps; the time
-    is the slowest process's wall clock around the timed steps."""
+    job's GPUs (one process per GPU), batch 1 and batch 16 at context ctx
+    (cache positions below ctx zero-filled, not decoded).  The wo / w2
+    partials are all-reduced by the quantizer that follows them, over peer
+    memory (NVLink); with more than one GPU the NCCL all-reduce
+    (LQ_TP_ALLREDUCE=nccl) is timed too, as the baseline.  Every process runs
+    the same steps; the time is the slowest process's wall clock around the
+    timed steps."""
     D, H, L, V = 8192, 28672, 80, 32000
     cfg = lq.Config.make(D, H, L, 64, 8, V, 4096)
-    gid = None
-    if world > 1:
-        buf = torch.zeros(128, dtype=torch.uint8, device="cuda")
-        if rank == 0:
-            buf.copy_(torch.frombuffer(bytearray(lq.tp_unique_id()), dtype=torch.uint8))
-        dist.broadcast(buf, 0)
-        gid = bytes(buf.cpu().numpy().tobytes())
-    t0 = time.perf_counter()
-    t = lq.Transformer.random_tp(cfg, lq.KIND_INT4, 64, 23, rank, world, gid, ctx + steps1 + 16)
-    init_s = time.perf_counter() - t0
     nmat = L * (2 * D * D + 2 * D * 1024 + 3 * D * H)
     wbytes = (nmat * 0.5 + nmat // 64 * 4) / world + V * D * (0.5 + 4 / 64)
-    runs = []
-    for B in (1, 16):
-        steps = steps1 if B == 1 else steps16
-        if B > 1:
-            t.reserve_batch(B)
-        tok = np.ones(B, np.int32)
-        for w in range(3):
-            tok = t.forward_batch_argmax(tok, np.full(B, ctx - 3 + w, np.int32))
-        if dist:
-            dist.barrier()
-        torch.cuda.synchronize()
-        t1 = time.perf_counter()
-        for s_ in range(steps):
-            tok = t.forward_batch_argmax(tok, np.full(B, ctx + s_, np.int32))
-        dt = (time.perf_counter() - t1) / steps
-        if dist:
-            m = torch.tensor([dt], device="cuda")
-            dist.all_reduce(m, op=dist.ReduceOp.MAX)
-            dt = float(m.item())
-        kv = B * 2 * L * (1024 / world) * 4 * (ctx + steps / 2)
-        runs.append({"batch": B, "tok_s": round(B / dt, 1), "ms_per_step": round(1e3 * dt, 3),
-                     "weight_bytes_per_gpu": int(wbytes), "kv_bytes_per_gpu_per_step": int(kv),
-                     "hbm_gbs_per_gpu": round((wbytes + kv) / dt / 1e9, 1),
-                     "path": "tcgen05 kind::i8" if B >= 16 else "dp4a GEMV"})
-    t.close()
-    return {"config": "config5: llama-2-70b shape, int4 gs64, tensor parallel x%d, context %d" % (world, ctx),
-            "split": "wq/wk/wv/w1/w3 rows, wo/w2 columns, NCCL all-reduce after wo and w2 (in the decode graph)",
-            "timing": "max over processes of the wall clock around the timed forward_batch_argmax calls",
-            "kv_note": "cache positions below the context are zero-filled, not decoded",
-            "init_s": round(init_s, 1), "runs": runs}
+
+    def measure(allreduce):
+        gid = None
+        if world > 1:
+            buf = torch.zeros(128, dtype=torch.uint8, device="cuda")
+            if rank == 0:
+                buf.copy_(torch.frombuffer(bytearray(lq.tp_unique_id()), dtype=torch.uint8))
+            dist.broadcast(buf, 0)
+            gid = bytes(buf.cpu().numpy().tobytes())
+        if allreduce:
+            os.environ["LQ_TP_ALLREDUCE"] = allreduce
+        else:
+            os.environ.pop("LQ_TP_ALLREDUCE", None)
+        t0 = time.perf_counter()
+        t = lq.Transformer.random_tp(cfg, lq.KIND_INT4, 64, 23, rank, world, gid, ctx + steps1 + 16)
+        init_s = time.perf_counter() - t0
+        os.environ.pop("LQ_TP_ALLREDUCE", None)
+        runs = []
+        for B in (1, 16):
+            steps = steps1 if B == 1 else steps16
+            if B > 1:
+                t.reserve_batch(B)
+            tok = np.ones(B, np.int32)
+            for w in range(3):
+                tok = t.forward_batch_argmax(tok, np.full(B, ctx - 3 + w, np.int32))
+            if dist:
+                dist.barrier()
+            torch.cuda.synchronize()
+            t1 = time.perf_counter()
+            for s_ in range(steps):
+                tok = t.forward_batch_argmax(tok, np.full(B, ctx + s_, np.int32))
+            dt = (time.perf_counter() - t1) / steps
+            if dist:
+                m = torch.tensor([dt], device="cuda")
+                dist.all_reduce(m, op=dist.ReduceOp.MAX)
+                dt = float(m.item())
+            kv = B * 2 * L * (1024 / world) * 4 * (ctx + steps / 2)
+            runs.append({"batch": B, "tok_s": round(B / dt, 1), "ms_per_step": round(1e3 * dt, 3),
+                         "weight_bytes_per_gpu": int(wbytes), "kv_bytes_per_gpu_per_step": int(kv),
+                         "hbm_gbs_per_gpu": round((wbytes + kv) / dt / 1e9, 1),
+                         "path": "tcgen05 kind::i8" if B >= 16 else "dp4a GEMV"})
+        t.close()
+        return runs, init_s
+
+    runs, init_s = measure(None)
+    out = {"config": "config5: llama-2-70b shape, int4 gs64, tensor parallel x%d, context %d" % (world, ctx),
+           "split": "wq/wk/wv/w1/w3 rows, wo/w2 columns; the wo / w2 partials are summed over the processes "
+                    "by the next quantizer, reading the peers' partials over NVLink (in the decode graph)",
+           "timing": "max over processes of the wall clock around the timed forward_batch_argmax calls",
+           "kv_note": "cache positions below the context are zero-filled, not decoded",
+           "init_s": round(init_s, 1), "runs": runs}
+    if world > 1:
+        nccl_runs, _ = measure("nccl")
+        out["nccl_allreduce_runs"] = [{"batch": r["batch"], "tok_s": r["tok_s"], "ms_per_step": r["ms_per_step"]}
+                                      for r in nccl_runs]
+    return out
 
 
 def probe(spec: str):

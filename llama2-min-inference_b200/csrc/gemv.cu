@@ -838,6 +838,55 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
 
 constexpr int kAqThreads = 256;
 
+// One task = 8 consecutive values of activation row b (gs/8 consecutive
+// tasks, inside one warp, form a quantization group): optional rmsnorm
+// scaling w * (inv * v), then quantize_act (runq.c:117-139) and store the
+// int8 values, the group scale and the group sum.
+__device__ __forceinline__ void quant_task8(const ActQuantArgs& a, int b, int task, bool on, bool norm, float inv,
+                                            float (&v)[8]) {
+    const int n = a.n, gs = a.gs, ng = n / gs;
+    const int lpg = gs / 8;
+    const int k0 = (on ? task : 0) * 8;
+    float amax = 0.0f;
+    if (on) {
+        if (norm) {
+            const float4 w0 = *reinterpret_cast<const float4*>(a.rms_w + k0);
+            const float4 w1 = *reinterpret_cast<const float4*>(a.rms_w + k0 + 4);
+            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = w[i] * (inv * v[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+    for (int o = 1; o < lpg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    float sc = amax / 127.0f;
+    if (sc == 0.0f) sc = 1e-8f;
+    const float rcp = 1.0f / sc;
+    int qs = 0;
+    if (on) {
+        int q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            q[i] = max(-127, min(127, quant_div(v[i], sc, rcp)));
+            qs += q[i];
+        }
+        const uint32_t lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+        const uint32_t hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+        *reinterpret_cast<uint2*>(a.xq + (size_t)b * n + k0) = make_uint2(lo, hi);
+    }
+    for (int o = 1; o < lpg; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+    if (on && (task & (lpg - 1)) == 0) {
+        const int g = task / lpg;
+        a.xs[(size_t)b * ng + g] = sc;
+        a.xsum[(size_t)b * ng + g] = qs;
+        if (a.xs_t) {
+            const int c = b >> 6, ld = c < a.xs_nfull ? 64 : a.xs_npad_last;
+            a.xs_t[(size_t)c * ng * 64 + (size_t)g * ld + (b & 63)] = sc * a.xs_t_mul;
+        }
+    }
+}
+
 __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_constant__ ActQuantArgs a) {
     __shared__ float red[kAqThreads / 32];
     pdl_trigger();
@@ -892,12 +941,10 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_cons
         for (int w = 0; w < kAqThreads / 32; ++w) t += red[w];
         inv = 1.0f / sqrtf(t / (float)n + 1e-5f);
     }
-    const int lpg = gs / 8;
     const int task = blockIdx.x * kAqThreads + ctid;  // 8 values per task
-    const bool on = task < ng * lpg;
+    const bool on = task < ng * (gs / 8);
     const int k0 = (on ? task : 0) * 8;
     float v[8];
-    float amax = 0.0f;
     if (on) {
         const float4 a0 = *reinterpret_cast<const float4*>(src + k0);
         const float4 a1 = *reinterpret_cast<const float4*>(src + k0 + 4);
@@ -909,42 +956,8 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_cons
             v[0] += y0.x; v[1] += y0.y; v[2] += y0.z; v[3] += y0.w;
             v[4] += y1.x; v[5] += y1.y; v[6] += y1.z; v[7] += y1.w;
         }
-        if (norm) {
-            const float4 w0 = *reinterpret_cast<const float4*>(a.rms_w + k0);
-            const float4 w1 = *reinterpret_cast<const float4*>(a.rms_w + k0 + 4);
-            const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = w[i] * (inv * v[i]);
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
     }
-    for (int o = 1; o < lpg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    float sc = amax / 127.0f;
-    if (sc == 0.0f) sc = 1e-8f;
-    const float rcp = 1.0f / sc;
-    int qs = 0;
-    if (on) {
-        int q[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            q[i] = max(-127, min(127, quant_div(v[i], sc, rcp)));
-            qs += q[i];
-        }
-        const uint32_t lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
-        const uint32_t hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
-        *reinterpret_cast<uint2*>(a.xq + (size_t)b * n + k0) = make_uint2(lo, hi);
-    }
-    for (int o = 1; o < lpg; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
-    if (on && (task & (lpg - 1)) == 0) {
-        const int g = task / lpg;
-        a.xs[(size_t)b * ng + g] = sc;
-        a.xsum[(size_t)b * ng + g] = qs;
-        if (a.xs_t) {
-            const int c = b >> 6, ld = c < a.xs_nfull ? 64 : a.xs_npad_last;
-            a.xs_t[(size_t)c * ng * 64 + (size_t)g * ld + (b & 63)] = sc * a.xs_t_mul;
-        }
-    }
+    quant_task8(a, b, task, on, norm, inv, v);
 }
 
 cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl) {
@@ -960,6 +973,118 @@ cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl) {
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, act_quant_kernel, a);
+}
+
+// ---------------------------------------------------------------------------
+// tensor-parallel all-reduce + residual add + rmsnorm + quantize (one CTA per
+// activation row; protocol in lq_kernels.h)
+
+constexpr int kPeerMaxN = 8192;  // one CTA of at most 1024 threads, 8 values each
+
+__global__ void __launch_bounds__(1024) peer_add_quant_kernel(const __grid_constant__ PeerAddArgs pa) {
+    extern __shared__ __align__(16) float srow[];  // x + y of this row [n]
+    __shared__ float red[kAqThreads / 32];
+    __shared__ uint32_t s_call;
+    const ActQuantArgs& a = pa.q;
+    pdl_trigger();
+    pdl_wait();  // this process's partial (the previous kernel's output) is complete
+    const int b = blockIdx.y, n = a.n, ctid = threadIdx.x;
+    if (ctid == 0) {
+        const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(&pa.counters[0]) + 1u;
+        s_call = e;
+        __threadfence();
+        if (b == 0) {
+            // publish: every write before this point (the partial) is ordered before the flag
+            fence_acq_rel_sys();
+            for (int p = 0; p < pa.tp_size; ++p)
+                if (p != pa.tp_rank) st_release_sys(pa.peer_flag[p], e);
+        }
+        // the last CTA to read the call number advances it for the next call
+        if (atomicAdd(&pa.counters[1], 1u) == gridDim.y - 1) {
+            pa.counters[1] = 0;
+            pa.counters[0] = e;
+        }
+    }
+    __syncthreads();
+    const uint32_t e = s_call;
+    if (ctid < pa.tp_size && ctid != pa.tp_rank) {
+        // bounded wait for peer ctid's partial of call e
+        const uint32_t* f = pa.my_flags + ctid;
+        if ((int)(ld_acquire_sys(f) - e) < 0) {
+            const uint64_t t0 = globaltimer();
+            for (uint32_t i = 1;; ++i) {
+                if ((int)(ld_acquire_sys(f) - e) >= 0) break;
+                if ((i & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+                    set_err(pa.err, DEV_TIMEOUT_PEER);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+    // y = sum of the partials in rank order, x_out = x + y (8 values per thread)
+    const int task = ctid;
+    const bool on = task < n / 8;
+    const int k0 = task * 8;
+    const size_t off = (size_t)b * n + k0;
+    float v[8];
+    if (on) {
+        float4 y0 = ld_volatile_f4(pa.peer_slot[0] + off), y1 = ld_volatile_f4(pa.peer_slot[0] + off + 4);
+        for (int p = 1; p < pa.tp_size; ++p) {
+            const float4 z0 = ld_volatile_f4(pa.peer_slot[p] + off), z1 = ld_volatile_f4(pa.peer_slot[p] + off + 4);
+            y0.x += z0.x; y0.y += z0.y; y0.z += z0.z; y0.w += z0.w;
+            y1.x += z1.x; y1.y += z1.y; y1.z += z1.z; y1.w += z1.w;
+        }
+        const float4 x0 = *reinterpret_cast<const float4*>(a.x + off);
+        const float4 x1 = *reinterpret_cast<const float4*>(a.x + off + 4);
+        v[0] = x0.x + y0.x; v[1] = x0.y + y0.y; v[2] = x0.z + y0.z; v[3] = x0.w + y0.w;
+        v[4] = x1.x + y1.x; v[5] = x1.y + y1.y; v[6] = x1.z + y1.z; v[7] = x1.w + y1.w;
+        const float4 r0 = make_float4(v[0], v[1], v[2], v[3]), r1 = make_float4(v[4], v[5], v[6], v[7]);
+        *reinterpret_cast<float4*>(a.x_out + off) = r0;
+        *reinterpret_cast<float4*>(a.x_out + off + 4) = r1;
+        *reinterpret_cast<float4*>(srow + k0) = r0;
+        *reinterpret_cast<float4*>(srow + k0 + 4) = r1;
+    }
+    __syncthreads();
+    // rmsnorm sum of squares in act_quant_kernel's order: 256 threads, thread
+    // t takes float4 chunks t, t+256, ...; warps summed in order
+    if (ctid < kAqThreads) {
+        float ss = 0.0f;
+        for (int c = ctid; c < n / 4; c += kAqThreads) {
+            const float4 q = reinterpret_cast<const float4*>(srow)[c];
+            ss = fmaf(q.x, q.x, ss);
+            ss = fmaf(q.y, q.y, ss);
+            ss = fmaf(q.z, q.z, ss);
+            ss = fmaf(q.w, q.w, ss);
+        }
+        ss = warp_sum(ss);
+        if ((ctid & 31) == 0) red[ctid >> 5] = ss;
+    }
+    __syncthreads();
+    float t = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kAqThreads / 32; ++w) t += red[w];
+    const float inv = 1.0f / sqrtf(t / (float)n + 1e-5f);
+    quant_task8(a, b, task, on, true, inv, v);
+}
+
+cudaError_t peer_add_quant_launch(const PeerAddArgs& a, cudaStream_t st, bool pdl) {
+    const int n = a.q.n;
+    if (!gs_ok_dev(a.q.gs) || n % a.q.gs || n % 8 || n > kPeerMaxN || a.tp_size < 1 || a.tp_size > kTpMax ||
+        a.q.nb < 1 || a.q.nb > kTpMaxRows)
+        return cudaErrorInvalidValue;
+    const int threads = kAqThreads * ((n / 8 + kAqThreads - 1) / kAqThreads);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(1, a.q.nb);
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = (size_t)n * sizeof(float);
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, peer_add_quant_kernel, a);
 }
 
 // ---------------------------------------------------------------------------

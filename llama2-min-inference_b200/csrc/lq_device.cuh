@@ -12,6 +12,7 @@ enum : int {
     DEV_TIMEOUT_FULL = 0x101,   // consumer waited too long for a stage to land
     DEV_TIMEOUT_EMPTY = 0x102,  // producer waited too long for a stage to drain
     DEV_TIMEOUT_DRAIN = 0x103,  // producer could not confirm its copies after an error
+    DEV_TIMEOUT_PEER = 0x104,   // a tensor-parallel peer did not publish its partial in time
     DEV_BAD_ARG = 0x201,        // a launch argument failed a device-side check
 };
 
@@ -114,6 +115,28 @@ __device__ __forceinline__ float warp_sum(float v) {
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// System-scope accesses for flags and data shared with peer GPUs.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+__device__ __forceinline__ float4 ld_volatile_f4(const float* p) {
+    float4 v;
+    asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "l"(p)
+                 : "memory");
     return v;
 }
 

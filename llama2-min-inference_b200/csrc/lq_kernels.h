@@ -117,6 +117,38 @@ struct ActQuantArgs {
 };
 cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl);
 
+// Tensor-parallel all-reduce fused into the quantizer that follows a wo / w2
+// product.  Each process owns an exchange region in its own device memory,
+// mapped by every peer (CUDA IPC):
+//   flags[kTpMax] (uint32, one per peer: the last call whose partial that
+//   peer has ready), counters[2] (this process only: calls done, CTAs
+//   arrived), then two partial slots of [kTpMaxRows][dim] fp32.
+// The products write their partial into this process's slot (wo: slot 0,
+// w2: slot 1, so the slots alternate call by call).  The quantizer then
+// publishes "partial ready for call e" to every peer, waits (bounded) until
+// every peer has published call e, and reads each peer's partial over
+// NVLink: y = ((y_0 + y_1) + y_2) ... in rank order on every process, x_out
+// = x + y, then rmsnorm + quantize exactly like act_quant_kernel's
+// IN_ADD_RMSNORM (same summation orders), so for two processes the result
+// equals the NCCL all-reduce path bit for bit.
+// A slot is rewritten two calls later, only after the writer has seen every
+// peer publish the call in between, which each peer does only after it has
+// finished reading the slot.
+constexpr int kTpMax = 8;
+constexpr int kTpMaxRows = 1024;
+constexpr int kXrFlagsBytes = 256;     // flags, padded
+constexpr int kXrCountersBytes = 256;  // counters, padded
+struct PeerAddArgs {
+    ActQuantArgs q;                    // mode IN_ADD_RMSNORM fields except y
+    const float* peer_slot[kTpMax];    // this call's slot of every process (rank order; own one included)
+    uint32_t* peer_flag[kTpMax];       // flags[tp_rank] in every peer's region (own entry unused)
+    const uint32_t* my_flags;          // this process's flags[kTpMax]
+    uint32_t* counters;                // this process's counters[2]
+    int tp_rank, tp_size;
+    int* err;
+};
+cudaError_t peer_add_quant_launch(const PeerAddArgs& a, cudaStream_t st, bool pdl);
+
 // Plan and launch.  pdl: allow programmatic dependent launch overlap with
 // the previous kernel on the stream.  Returns a cudaError_t.
 cudaError_t gemv_launch(GemvArgs a, int kind, cudaStream_t st, bool pdl, int num_sms);

@@ -47,6 +47,12 @@ struct Transformer {
     void* comm = nullptr;                // NCCL communicator (tp_size > 1)
     int nh_l = 0, nkv_l = 0, dq_l = 0, hid_l = 0;  // local query heads, kv heads, q width, hidden rows
     float *x2 = nullptr, *ybuf = nullptr;  // second residual buffer; all-reduced partial [B][dim]
+    // peer all-reduce (tp_size > 1): this process's exchange region and every
+    // process's region as mapped here (rank order, own one included); with
+    // tp_nccl set (LQ_TP_ALLREDUCE=nccl) the step all-reduces ybuf with NCCL
+    void* xr = nullptr;
+    void* xr_peer[8] = {};
+    bool tp_nccl = false;
     // tensor-core GEMM path (steps of mma_min or more sequences)
     int mma_min = 16;
     int xs_ld = 0;                       // max_batch rounded up to 64 (xs_t: a [groups][64] table per 64 rows)

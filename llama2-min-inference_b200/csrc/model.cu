@@ -40,12 +40,16 @@ namespace {
 
 int64_t rbytes(int64_t cols, int kind) { return kind == LQ_KIND_INT8 ? cols : cols / 2; }
 
+// one partial slot of the peer all-reduce exchange region: [kTpMaxRows][dim] fp32
+size_t xr_slot_bytes(const Transformer* t) { return (size_t)lq::kTpMaxRows * t->c.dim * sizeof(float); }
+
 // NCCL, opened on first use: the copy a host framework already loaded
 // (torch's) when there is one, else the system's libnccl.so.2
 struct Nccl {
     ncclResult_t (*get_unique_id)(ncclUniqueId*);
     ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int);
     ncclResult_t (*all_reduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
     ncclResult_t (*comm_destroy)(ncclComm_t);
     const char* (*error_string)(ncclResult_t);
 };
@@ -61,9 +65,11 @@ const Nccl* nccl() {
             f.get_unique_id = reinterpret_cast<decltype(f.get_unique_id)>(dlsym(h, "ncclGetUniqueId"));
             f.comm_init_rank = reinterpret_cast<decltype(f.comm_init_rank)>(dlsym(h, "ncclCommInitRank"));
             f.all_reduce = reinterpret_cast<decltype(f.all_reduce)>(dlsym(h, "ncclAllReduce"));
+            f.all_gather = reinterpret_cast<decltype(f.all_gather)>(dlsym(h, "ncclAllGather"));
             f.comm_destroy = reinterpret_cast<decltype(f.comm_destroy)>(dlsym(h, "ncclCommDestroy"));
             f.error_string = reinterpret_cast<decltype(f.error_string)>(dlsym(h, "ncclGetErrorString"));
-            if (f.get_unique_id && f.comm_init_rank && f.all_reduce && f.comm_destroy && f.error_string) state = 1;
+            if (f.get_unique_id && f.comm_init_rank && f.all_reduce && f.all_gather && f.comm_destroy && f.error_string)
+                state = 1;
         }
     }
     return state == 1 ? &f : nullptr;
@@ -120,6 +126,8 @@ int check_config(const Config* c, int gs, int tp_size = 1) {
         if (c->n_kv_heads % tp_size || c->n_heads % tp_size)
             return lq_fail(LQ_EINVAL, "tensor parallelism: %d query / %d kv heads do not split over %d GPUs",
                            c->n_heads, c->n_kv_heads, tp_size);
+        if (c->dim > 8192)
+            return lq_fail(LQ_EUNSUPPORTED, "tensor parallelism: dim %d above 8192 (one quantizer CTA per row)", c->dim);
         if ((c->dim / tp_size) % gs || (c->hidden_dim / tp_size) % gs || c->hidden_dim % tp_size)
             return lq_fail(LQ_EINVAL, "tensor parallelism: dim/%d and hidden_dim/%d must be multiples of gs=%d",
                            tp_size, tp_size, gs);
@@ -377,11 +385,52 @@ int forward_launch(Transformer* t, int batch) {
     // columns; they are all-reduced and added to the residual stream by the
     // next quantizer, which reads one residual buffer and writes the other
     auto allreduce = [&]() -> int {
-        if (t->tp_size == 1) return LQ_OK;
+        if (t->tp_size == 1 || !t->tp_nccl) return LQ_OK;
         const ncclResult_t r = nccl()->all_reduce(t->ybuf, t->ybuf, (size_t)batch * D, ncclFloat, ncclSum,
                                                   static_cast<ncclComm_t>(t->comm), st);
         return r == ncclSuccess ? LQ_OK : lq_fail(LQ_ECUDA, "all-reduce: %s", nccl()->error_string(r));
     };
+    // peer all-reduce: wo writes its partial to slot 0 of this process's
+    // exchange region, w2 to slot 1; the next quantizer reduces over the peers
+    const bool peer = t->tp_size > 1 && !t->tp_nccl;
+    auto slot = [&](int k) -> float* {
+        return reinterpret_cast<float*>(static_cast<char*>(t->xr) + kXrFlagsBytes + kXrCountersBytes +
+                                        k * xr_slot_bytes(t));
+    };
+    auto add_quant = [&](const float* x, const float* rms_w, float* x_out, int k) -> cudaError_t {
+        if (!peer) return quant(IN_ADD_RMSNORM, x, D, rms_w, x_out, t->ybuf);
+        PeerAddArgs p{};
+        // the quantizer fields as quant() fills them
+        p.q.mode = IN_ADD_RMSNORM;
+        p.q.n = D;
+        p.q.gs = gs;
+        p.q.nb = batch;
+        p.q.x = x;
+        p.q.rms_w = rms_w;
+        p.q.x_out = x_out;
+        p.q.xq = t->xq;
+        p.q.xs = t->xqs;
+        p.q.xsum = t->xqsum;
+        if (use_mma(t, batch)) {
+            p.q.xs_t = t->xs_t;
+            p.q.xs_nfull = batch / 64;
+            p.q.xs_npad_last = batch % 64 ? qgemm_npad(batch % 64) : 64;
+            p.q.xs_t_mul = kind == LQ_KIND_INT4 ? 0.0625f : 1.0f;
+        }
+        for (int r = 0; r < t->tp_size; ++r) {
+            char* base = static_cast<char*>(t->xr_peer[r]);
+            p.peer_slot[r] = reinterpret_cast<const float*>(base + kXrFlagsBytes + kXrCountersBytes + k * xr_slot_bytes(t));
+            p.peer_flag[r] = reinterpret_cast<uint32_t*>(base) + t->tp_rank;
+        }
+        p.my_flags = static_cast<const uint32_t*>(t->xr);
+        p.counters = reinterpret_cast<uint32_t*>(static_cast<char*>(t->xr) + kXrFlagsBytes);
+        p.tp_rank = t->tp_rank;
+        p.tp_size = t->tp_size;
+        p.err = t->err;
+        return peer_add_quant_launch(p, st, true);
+    };
+    float* ywo = peer ? slot(0) : t->ybuf;  // where the partial products go
+    float* yw2 = peer ? slot(1) : t->ybuf;
     float* xa = t->x;              // residual stream after attention's add (and the embedding)
     float* xb = t->tp ? t->x2 : t->x;  // after the ffn's add
     int rc;
@@ -392,7 +441,7 @@ int forward_launch(Transformer* t, int batch) {
         if (l == 0)
             e = quant(IN_RMSNORM_EMB, xa, D, rms_a, xa);
         else if (t->tp)
-            e = quant(IN_ADD_RMSNORM, xb, D, rms_a, xa, t->ybuf);
+            e = add_quant(xb, rms_a, xa, 1);
         else
             e = quant(IN_RMSNORM, xa, D, rms_a);
         if (e != cudaSuccess) return cuda_fail(e, "attention rmsnorm");
@@ -428,7 +477,7 @@ int forward_launch(Transformer* t, int batch) {
         // 3. wo + residual
         if ((e = quant(IN_F32, t->att, DQ, nullptr)) != cudaSuccess) return cuda_fail(e, "attention output quantize");
         base(a, DQ);
-        a.seg[0] = {t->wo.q + (size_t)l * D * rbQ, t->wo.s + (size_t)l * D * ngQ, t->tp ? t->ybuf : xa, D,
+        a.seg[0] = {t->wo.q + (size_t)l * D * rbQ, t->wo.s + (size_t)l * D * ngQ, t->tp ? ywo : xa, D,
                     t->tp ? EPI_STORE : EPI_ADD};
         a.nseg = 1;
         qin(a);
@@ -436,7 +485,7 @@ int forward_launch(Transformer* t, int batch) {
         if ((rc = allreduce())) return rc;
         // 4. w1 | w3 paired, SwiGLU in the epilogue: h1 = silu(x.w1) * (x.w3)
         const float* rms_f = t->rms_ffn + (size_t)l * D;
-        e = t->tp ? quant(IN_ADD_RMSNORM, xa, D, rms_f, xb, t->ybuf) : quant(IN_RMSNORM, xa, D, rms_f);
+        e = t->tp ? add_quant(xa, rms_f, xb, 0) : quant(IN_RMSNORM, xa, D, rms_f);
         if (e != cudaSuccess) return cuda_fail(e, "ffn rmsnorm");
         base(a, D);
         a.seg[0] = {t->w1.q + (size_t)l * H * rbD, t->w1.s + (size_t)l * H * ngD, t->h1, H, EPI_SWIGLU,
@@ -449,7 +498,7 @@ int forward_launch(Transformer* t, int batch) {
         // 5. w2 + residual
         if ((e = quant(IN_F32, t->h1, H, nullptr)) != cudaSuccess) return cuda_fail(e, "ffn quantize");
         base(a, H);
-        a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->tp ? t->ybuf : xb, D,
+        a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->tp ? yw2 : xb, D,
                     t->tp ? EPI_STORE : EPI_ADD};
         a.nseg = 1;
         qin(a);
@@ -457,7 +506,7 @@ int forward_launch(Transformer* t, int batch) {
         if ((rc = allreduce())) return rc;
     }
     GemvArgs a;
-    e = t->tp ? quant(IN_ADD_RMSNORM, xb, D, t->rms_final, xa, t->ybuf) : quant(IN_RMSNORM, xa, D, t->rms_final);
+    e = t->tp ? add_quant(xb, t->rms_final, xa, 1) : quant(IN_RMSNORM, xa, D, t->rms_final);
     if (e != cudaSuccess) return cuda_fail(e, "final rmsnorm");
     base(a, D);
     a.seg[0] = {t->wcls.q, t->wcls.s, t->logits, c.vocab_size, EPI_STORE};
@@ -567,6 +616,74 @@ void tp_local_shape(const Transformer* t, const LqTensorDesc& d, int64_t* rows, 
     if (tp_split(d.id) == 2) *cols = d.cols / t->tp_size;
 }
 
+// Peer all-reduce setup (collective): allocate and zero this process's
+// exchange region, export it (CUDA IPC), gather every process's handle with
+// one NCCL all-gather and map the peers' regions.  The all-gather completes
+// only after every process has zeroed its region, so no flag is written
+// before its owner has cleared it.
+int xr_setup(Transformer* t) {
+    const int size = t->tp_size, rank = t->tp_rank;
+    if (size > lq::kTpMax) return lq_fail(LQ_EUNSUPPORTED, "peer all-reduce over %d GPUs (at most %d)", size, lq::kTpMax);
+    const size_t bytes = lq::kXrFlagsBytes + lq::kXrCountersBytes + 2 * xr_slot_bytes(t);
+    cudaError_t e = cudaMalloc(&t->xr, bytes);
+    if (e != cudaSuccess) return cuda_fail(e, "exchange region");
+    cudaStream_t st = nullptr;
+    char* hbuf = nullptr;
+    cudaIpcMemHandle_t own;
+    e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaMemsetAsync(t->xr, 0, bytes, st);
+    if (e == cudaSuccess) e = cudaIpcGetMemHandle(&own, t->xr);
+    if (e == cudaSuccess) e = cudaMalloc(&hbuf, sizeof(cudaIpcMemHandle_t) * size);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(hbuf + sizeof(own) * rank, &own, sizeof(own), cudaMemcpyHostToDevice, st);
+    int rc = e == cudaSuccess ? LQ_OK : cuda_fail(e, "exchange region export");
+    if (!rc) {
+        const ncclResult_t r = nccl()->all_gather(hbuf + sizeof(own) * rank, hbuf, sizeof(own), ncclChar,
+                                                  static_cast<ncclComm_t>(t->comm), st);
+        if (r != ncclSuccess) rc = lq_fail(LQ_ECUDA, "exchange handle all-gather: %s", nccl()->error_string(r));
+    }
+    std::vector<cudaIpcMemHandle_t> all(size);
+    if (!rc) {
+        e = cudaMemcpyAsync(all.data(), hbuf, sizeof(own) * size, cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) rc = cuda_fail(e, "exchange handle all-gather");
+    }
+    for (int p = 0; p < size && !rc; ++p) {
+        if (p == rank) {
+            t->xr_peer[p] = t->xr;
+            continue;
+        }
+        e = cudaIpcOpenMemHandle(&t->xr_peer[p], all[p], cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) rc = cuda_fail(e, "mapping a peer's exchange region");
+    }
+    if (hbuf) cudaFree(hbuf);
+    if (st) cudaStreamDestroy(st);
+    return rc;
+}
+
+// Undo xr_setup.  Collective: one NCCL all-reduce first, so that every
+// process has finished every step (whose kernels read the peers' regions)
+// before any region is unmapped or freed.
+void xr_teardown(Transformer* t) {
+    if (!t->xr) return;
+    bool synced = false;
+    if (t->comm && t->stream) {
+        float* one = nullptr;
+        if (cudaMalloc(&one, sizeof(float)) == cudaSuccess) {
+            synced = nccl()->all_reduce(one, one, 1, ncclFloat, ncclSum, static_cast<ncclComm_t>(t->comm), t->stream) ==
+                         ncclSuccess &&
+                     cudaStreamSynchronize(t->stream) == cudaSuccess;
+            cudaFree(one);
+        }
+    }
+    for (int p = 0; p < t->tp_size && p < lq::kTpMax; ++p)
+        if (t->xr_peer[p] && p != t->tp_rank) cudaIpcCloseMemHandle(t->xr_peer[p]);
+    for (void*& q : t->xr_peer) q = nullptr;
+    // without the barrier a peer may still read this region: leave it allocated
+    if (synced) cudaFree(t->xr);
+    t->xr = nullptr;
+}
+
 int tp_join(Transformer* t, int rank, int size, const void* id) {
     t->tp = true;
     t->tp_rank = rank;
@@ -580,7 +697,8 @@ int tp_join(Transformer* t, int rank, int size, const void* id) {
     const ncclResult_t r = f->comm_init_rank(&comm, size, uid, rank);
     if (r != ncclSuccess) return lq_fail(LQ_ECUDA, "NCCL communicator (rank %d of %d): %s", rank, size, f->error_string(r));
     t->comm = comm;
-    return LQ_OK;
+    if (const char* m = getenv("LQ_TP_ALLREDUCE")) t->tp_nccl = strcmp(m, "nccl") == 0;
+    return t->tp_nccl ? LQ_OK : xr_setup(t);
 }
 
 // Read the checkpoint's tensors (mmap'd at data + hb) into t, this process's
@@ -790,7 +908,8 @@ int lq_tp_unique_id(void* id) {
 }
 
 static int tp_args_ok(int rank, int size, const void* id) {
-    if (size < 1 || size > 64 || rank < 0 || rank >= size) return lq_fail(LQ_EINVAL, "tp rank %d of %d", rank, size);
+    if (size < 1 || size > lq::kTpMax || rank < 0 || rank >= size)
+        return lq_fail(LQ_EINVAL, "tp rank %d of %d (at most %d processes)", rank, size, lq::kTpMax);
     if (size > 1 && !id) return lq_fail(LQ_EINVAL, "tensor parallelism over %d GPUs needs the group id", size);
     return LQ_OK;
 }
@@ -827,6 +946,7 @@ int forward_argmax(Transformer* t, int token, int pos, int* next_token) {
 void free_transformer(Transformer* t) {
     if (!t) return;
     free_state(t);  // the captured graph (which holds the all-reduces) goes before the communicator
+    xr_teardown(t);
     if (t->comm && nccl()) nccl()->comm_destroy(static_cast<ncclComm_t>(t->comm));
     t->comm = nullptr;
     QW* ws[] = {&t->wq, &t->wk, &t->wv, &t->wo, &t->w1, &t->w2, &t->w3, &t->wcls};

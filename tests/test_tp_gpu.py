@@ -45,10 +45,12 @@ def test_tp_structure_on_one_gpu_equals_plain_step(cuda, kind):
     b.close()
 
 
-def _tp_rank(rank, world, gid, kind, q):
+def _tp_rank(rank, world, gid, kind, q, allreduce=None):
     import importlib
     import sys
 
+    if allreduce:
+        os.environ["LQ_TP_ALLREDUCE"] = allreduce
     sys.path.insert(0, os.getcwd())
     L = importlib.import_module("llama2-min-inference_b200")
     L.lib()
@@ -62,16 +64,13 @@ def _tp_rank(rank, world, gid, kind, q):
     q.put((rank, out, outb))
 
 
-@pytest.mark.parametrize("kind", [8, 4])
-def test_tp_two_gpus_track_one_gpu(cuda, kind):
-    if cuda.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+def _run_pair(kind, allreduce=None):
     import multiprocessing as mp
 
     gid = lq.tp_unique_id()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_tp_rank, args=(r, 2, gid, kind, q)) for r in range(2)]
+    procs = [ctx.Process(target=_tp_rank, args=(r, 2, gid, kind, q, allreduce)) for r in range(2)]
     for p in procs:
         p.start()
     got = {}
@@ -81,6 +80,14 @@ def test_tp_two_gpus_track_one_gpu(cuda, kind):
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
+    return got
+
+
+@pytest.mark.parametrize("kind", [8, 4])
+def test_tp_two_gpus_track_one_gpu(cuda, kind):
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    got = _run_pair(kind)
     assert np.array_equal(got[0][0], got[1][0]) and np.array_equal(got[0][1], got[1][1])
     ref = lq.Transformer.random(_cfg(), kind, 64, SEED, 64)
     agree = 0
@@ -91,3 +98,16 @@ def test_tp_two_gpus_track_one_gpu(cuda, kind):
         agree += int(np.argmax(want) == np.argmax(got[0][0][pos]))
     assert agree >= len(TOKENS) - 1
     ref.close()
+
+
+@pytest.mark.parametrize("kind", [8, 4])
+def test_tp_peer_allreduce_equals_nccl(cuda, kind):
+    """Batch 1 (GEMV) and batch 16 (tensor-core GEMM) steps: the peer
+    all-reduce fused into the quantizer equals the NCCL all-reduce bitwise."""
+    if cuda.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    peer = _run_pair(kind)
+    ref = _run_pair(kind, "nccl")
+    for r in range(2):
+        for a, b in zip(peer[r], ref[r]):
+            assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (r, float(np.abs(a - b).max()))
