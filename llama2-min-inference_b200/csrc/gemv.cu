@@ -687,7 +687,9 @@ __device__ __forceinline__ void smem_rows_dot(const uint8_t* const* w, const flo
     }
 }
 
-template <int KIND, int NB, int CPG>
+// SPLIT / PAIRED: the launch's a.split and a.paired, fixed per instantiation
+// so that each kernel holds only the one dot loop it runs
+template <int KIND, int NB, int CPG, bool SPLIT, bool PAIRED>
 __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __grid_constant__ GemvArgs a, int prefetch) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_trigger();
@@ -701,7 +703,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
     const int rb = KIND == 8 ? n : n / 2;
     const int gb = KIND == 8 ? a.gs : a.gs / 2;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int tw = a.paired ? kSlotW / 2 : kSlotW;  // weight bytes per tensor in a slot
+    const int tw = PAIRED ? kSlotW / 2 : kSlotW;  // weight bytes per tensor in a slot
     int P = 0;
     for (int i = 0; i < a.nseg; ++i) P += a.seg[i].rows >> 1;
     const int nw = blockDim.x >> 5;
@@ -750,7 +752,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
         const uint8_t* sw = slots + (size_t)s * L.stage_bytes;
         const float* ss = reinterpret_cast<const float*>(sw + kSlotW);
         const GemvSeg& g = a.seg[it.seg];
-        if (!a.split) {
+        if (!SPLIT) {
             const float* ss2 = ss + it.nrows * ng;
             for (int r = 0; r < it.nrows; r += 2) {
                 float v[4][NB];
@@ -758,7 +760,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
                 for (int q = 0; q < 4; ++q)
 #pragma unroll
                     for (int b = 0; b < NB; ++b) v[q][b] = 0.0f;
-                if (a.paired) {
+                if (PAIRED) {
                     const uint8_t* wr[4] = {sw + (size_t)r * rb, sw + (size_t)(r + 1) * rb, sw + tw + (size_t)r * rb,
                                             sw + tw + (size_t)(r + 1) * rb};
                     const float* sr[4] = {ss + (size_t)r * ng, ss + (size_t)(r + 1) * ng, ss2 + (size_t)r * ng,
@@ -780,7 +782,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
             }
         } else {
             const int g0 = it.boff / gb, ngs = it.bytes / gb;
-            const int mult = a.paired ? 2 : 1;
+            const int mult = PAIRED ? 2 : 1;
             const int region = a.scap / (2 * mult);
             const uint8_t* sb = reinterpret_cast<const uint8_t*>(ss);
             float tmp[4][NB];
@@ -788,7 +790,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
             for (int q = 0; q < 4; ++q)
 #pragma unroll
                 for (int b = 0; b < NB; ++b) tmp[q][b] = 0.0f;
-            if (a.paired) {
+            if (PAIRED) {
                 const uint8_t* wr[4] = {sw, sw + tw / 2, sw + tw, sw + tw + tw / 2};
                 const float* sr[4] = {reinterpret_cast<const float*>(sb), reinterpret_cast<const float*>(sb + region),
                                       reinterpret_cast<const float*>(sb + 2 * region),
@@ -1149,12 +1151,15 @@ static cudaError_t launch_tma(GemvArgs a, cudaStream_t st, bool pdl, int num_sms
     if (!nw) return cudaErrorInvalidValue;
     a.nstages = 2 * nw;
     const Layout L = make_layout(a);
-    auto kern = gemv_tma_kernel<KIND, NB, CPG>;
-    static int set_bytes = 0;
-    if (L.total > set_bytes) {
+    void (*kern)(GemvArgs, int) = a.split ? (a.paired ? gemv_tma_kernel<KIND, NB, CPG, true, true>
+                                                     : gemv_tma_kernel<KIND, NB, CPG, true, false>)
+                                          : (a.paired ? gemv_tma_kernel<KIND, NB, CPG, false, true>
+                                                      : gemv_tma_kernel<KIND, NB, CPG, false, false>);
+    static bool attr_set[2][2] = {};
+    if (!attr_set[a.split][a.paired]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return e;
-        set_bytes = 227 * 1024;
+        attr_set[a.split][a.paired] = true;
     }
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
