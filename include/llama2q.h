@@ -204,11 +204,17 @@ int forward_batch_argmax(Transformer* t, const int* tokens, const int* pos, int 
  * w3 (its n_heads/tp_size query heads, n_kv_heads/tp_size kv heads and
  * hidden_dim/tp_size FFN rows) and the matching input columns of wo and w2.
  * Attention, RoPE, the KV cache and SwiGLU stay local; the wo and w2 products
- * are partial sums that one NCCL all-reduce per product (two per layer)
- * completes, inside the captured decode graph.  The embedding, the norms and
- * the classifier are replicated, so every process returns the full logits.
- * Every process calls forward / forward_argmax / forward_batch with the same
- * tokens and positions. */
+ * are partial sums, completed by an all-reduce per product (two per layer)
+ * inside the captured decode graph.  The all-reduce is fused into the next
+ * activation quantizer: it reads the peers' partials from their device memory
+ * over NVLink (CUDA IPC mappings set up when the model is built).  Setting
+ * LQ_TP_ALLREDUCE=nccl before building selects an ncclAllReduce instead.  At
+ * most 8 processes, dim at most 8192, at most 1024 sequences a step.  The
+ * embedding, the norms and the classifier are replicated, so every process
+ * returns the full logits.  Every process calls forward / forward_argmax /
+ * forward_batch / transformer_reserve_batch with the same arguments, and
+ * free_transformer at the end: for tp_size > 1 it waits for the whole group
+ * before the exchange memory is unmapped. */
 
 /* Create the group id (128 bytes) on one process; the caller hands it to the
  * others (a file, a socket, torch.distributed, ...). */
