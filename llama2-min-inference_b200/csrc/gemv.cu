@@ -1031,12 +1031,24 @@ __global__ void __launch_bounds__(1024) peer_add_quant_kernel(const __grid_const
     const size_t off = (size_t)b * n + k0;
     float v[8];
     if (on) {
-        float4 y0 = ld_volatile_f4(pa.peer_slot[0] + off), y1 = ld_volatile_f4(pa.peer_slot[0] + off + 4);
-        for (int p = 1; p < pa.tp_size; ++p) {
-            const float4 z0 = ld_volatile_f4(pa.peer_slot[p] + off), z1 = ld_volatile_f4(pa.peer_slot[p] + off + 4);
-            y0.x += z0.x; y0.y += z0.y; y0.z += z0.z; y0.w += z0.w;
-            y1.x += z1.x; y1.y += z1.y; y1.z += z1.z; y1.w += z1.w;
+        // every peer's loads of one half (4 values) are issued before the
+        // first add, so the NVLink round trips overlap; the adds run in rank order
+        float4 yh[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            float4 z[kTpMax];
+#pragma unroll
+            for (int p = 0; p < kTpMax; ++p)
+                if (p < pa.tp_size) z[p] = ld_volatile_f4(pa.peer_slot[p] + off + 4 * h);
+            float4 y = z[0];
+#pragma unroll
+            for (int p = 1; p < kTpMax; ++p)
+                if (p < pa.tp_size) {
+                    y.x += z[p].x; y.y += z[p].y; y.z += z[p].z; y.w += z[p].w;
+                }
+            yh[h] = y;
         }
+        const float4 y0 = yh[0], y1 = yh[1];
         const float4 x0 = *reinterpret_cast<const float4*>(a.x + off);
         const float4 x1 = *reinterpret_cast<const float4*>(a.x + off + 4);
         v[0] = x0.x + y0.x; v[1] = x0.y + y0.y; v[2] = x0.z + y0.z; v[3] = x0.w + y0.w;
