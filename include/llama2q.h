@@ -75,7 +75,11 @@ const char* lq_last_error(void);
 int lq_select_device(int device);
 int lq_set_stream(void* cuda_stream); /* cudaStream_t; NULL = legacy default */
 void* lq_get_stream(void);
-/* Synchronize the stream and report any device-side error word. */
+/* Synchronize the stream and report (then clear) the device-side error
+ * words of the operator calls on the current device: the context's, and the
+ * fixed scratch's when matmul_f32_noalloc has been used there.  A bounded
+ * device wait that gave up in any earlier call makes this return
+ * LQ_ETIMEOUT. */
 int lq_sync(void);
 
 /* Launch flags for the operator entry points.  LQ_LAUNCH_PDL lets each
@@ -145,7 +149,9 @@ int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int
  * library until exit: n is limited to 32768 (larger n returns LQ_EINVAL),
  * every call on a device shares the array, and calls whose kernels overlap
  * on the GPU race on it.  The first call on a device looks up the array's
- * address; make that call before any stream capture. */
+ * address; make that call before any stream capture.  A device-side error
+ * of these calls (a bounded wait that gave up) is kept in the array until
+ * the next lq_sync() reports it. */
 int matmul_f32_noalloc(float* xout, const float* x, const QuantizedTensor* w, int n, int d);
 
 /* ---- model ------------------------------------------------------------- */
@@ -228,6 +234,19 @@ int build_transformer_tp(Transformer** t, const char* checkpoint_path, int max_s
                          const void* id128);
 int build_transformer_random_tp(Transformer** t, const Config* cfg, int kind, int group_size, uint64_t seed,
                                 int max_seq_len, int tp_rank, int tp_size, const void* id128);
+
+/* Self-test of the failure path of the tensor-parallel all-reduce (no
+ * counterpart in the reference, which has one device).  Runs the fused
+ * all-reduce quantizer as rank 0 of a tp_size-process group (2..8) whose
+ * other members never publish their partials, with a wait limit of wait_us
+ * microseconds, twice in a row on the current device.  The first call's
+ * bounded wait gives up and records the error; the second call sees the
+ * recorded error and does not wait again.  Returns LQ_ETIMEOUT (the status a
+ * decode step returns when a peer stops taking part) and the two calls'
+ * device times in *first_ms / *second_ms (either may be NULL).  In a model
+ * the limit is 2 s, or LQ_TP_WAIT_MS milliseconds when that is set before
+ * the model is built. */
+int lq_tp_wait_selftest(int tp_size, int wait_us, double* first_ms, double* second_ms);
 
 /* Release a model (free_transformer, runq.c:285-289). */
 void free_transformer(Transformer* t);

@@ -83,7 +83,7 @@ EXPORTS = (
     "lq_synth_tensor", "quantize", "matmul", "matmul_f32", "matmul_f32_noalloc",
     "build_transformer", "build_transformer_random", "forward", "forward_argmax",
     "transformer_reserve_batch", "forward_batch", "forward_batch_argmax",
-    "lq_tp_unique_id", "build_transformer_tp", "build_transformer_random_tp",
+    "lq_tp_unique_id", "build_transformer_tp", "build_transformer_random_tp", "lq_tp_wait_selftest",
     "free_transformer", "transformer_config",
     "lq_write_checkpoint_fp32", "lq_quantize_checkpoint", "lq_read_header", "lq_synth_value",
 )
@@ -125,6 +125,7 @@ def lib() -> C.CDLL:
         "forward_argmax": (I, [P, I, I, C.POINTER(I)]),
         "transformer_reserve_batch": (I, [P, I]),
         "lq_tp_unique_id": (I, [P]),
+        "lq_tp_wait_selftest": (I, [I, I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
         "build_transformer_tp": (I, [C.POINTER(P), C.c_char_p, I, I, I, P]),
         "build_transformer_random_tp": (I, [C.POINTER(P), CFG, I, I, U64, I, I, I, P]),
         "forward_batch": (C.POINTER(F), [P, P, P, I]),
@@ -319,6 +320,14 @@ class Transformer:
             self.close()
         except Exception:
             pass
+
+
+def tp_wait_selftest(tp_size: int, wait_us: int):
+    """Run the all-reduce wait's failure path on this device (see the header):
+    returns (status code, first call ms, second call ms); LQ_ETIMEOUT expected."""
+    a, b = C.c_double(), C.c_double()
+    rc = lib().lq_tp_wait_selftest(tp_size, wait_us, C.byref(a), C.byref(b))
+    return rc, a.value, b.value
 
 
 def tp_unique_id() -> bytes:

@@ -174,7 +174,9 @@ void* lq_get_stream(void) { return g_stream; }
 int lq_sync(void) {
     DevCtx* c = ctx();
     if (!c) return lq_fail(LQ_ECUDA, "no CUDA device context (no device, or first use inside a graph capture)");
-    return check_device_error(c->err, g_stream);
+    const int a = check_device_error(c->err, g_stream);
+    const int b = noalloc_check_error(g_stream);  // always read (and clear) both words
+    return a ? a : b;
 }
 
 int lq_set_launch_flags(int flags) {

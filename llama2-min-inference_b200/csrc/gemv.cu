@@ -995,12 +995,13 @@ __global__ void __launch_bounds__(1024) peer_add_quant_kernel(const __grid_const
         const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(&pa.counters[0]) + 1u;
         s_call = e;
         __threadfence();
-        if (b == 0) {
-            // publish: every write before this point (the partial) is ordered before the flag
-            fence_acq_rel_sys();
-            for (int p = 0; p < pa.tp_size; ++p)
-                if (p != pa.tp_rank) st_release_sys(pa.peer_flag[p], e);
-        }
+        // publish: the previous kernel (this process's partial) completed
+        // before griddepcontrol.wait returned, so any CTA may order it before
+        // the flag; every CTA stores the same value, so none waits on another
+        // CTA being scheduled
+        fence_acq_rel_sys();
+        for (int p = 0; p < pa.tp_size; ++p)
+            if (p != pa.tp_rank) st_release_sys(pa.peer_flag[p], e);
         // the last CTA to read the call number advances it for the next call
         if (atomicAdd(&pa.counters[1], 1u) == gridDim.y - 1) {
             pa.counters[1] = 0;
@@ -1009,14 +1010,20 @@ __global__ void __launch_bounds__(1024) peer_add_quant_kernel(const __grid_const
     }
     __syncthreads();
     const uint32_t e = s_call;
-    if (ctid < pa.tp_size && ctid != pa.tp_rank) {
+    // once a wait has given up (this call or an earlier one of the step), the
+    // step's result is void: skip further waits so the host hears of it
+    // after one limit, not one per call
+    const bool failed = *reinterpret_cast<volatile const int*>(pa.err) != 0;
+    if (ctid < pa.tp_size && ctid != pa.tp_rank && !failed) {
         // bounded wait for peer ctid's partial of call e
         const uint32_t* f = pa.my_flags + ctid;
+        const uint64_t limit = pa.wait_ns ? pa.wait_ns : kWaitLimitNs;
         if ((int)(ld_acquire_sys(f) - e) < 0) {
             const uint64_t t0 = globaltimer();
             for (uint32_t i = 1;; ++i) {
                 if ((int)(ld_acquire_sys(f) - e) >= 0) break;
-                if ((i & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+                if ((i & 63u) == 0 && (globaltimer() - t0 > limit ||
+                                        *reinterpret_cast<volatile const int*>(pa.err) != 0)) {
                     set_err(pa.err, DEV_TIMEOUT_PEER);
                     break;
                 }

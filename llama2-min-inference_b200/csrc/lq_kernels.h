@@ -146,6 +146,7 @@ struct PeerAddArgs {
     uint32_t* counters;                // this process's counters[2]
     int tp_rank, tp_size;
     int* err;
+    uint64_t wait_ns;                  // limit of the wait for the peers' flags (0: the default 2 s)
 };
 cudaError_t peer_add_quant_launch(const PeerAddArgs& a, cudaStream_t st, bool pdl);
 

@@ -53,6 +53,7 @@ struct Transformer {
     void* xr = nullptr;
     void* xr_peer[8] = {};
     bool tp_nccl = false;
+    uint64_t tp_wait_ns = 0;             // peer flag wait limit (LQ_TP_WAIT_MS; 0 = the 2 s default)
     // tensor-core GEMM path (steps of mma_min or more sequences)
     int mma_min = 16;
     int xs_ld = 0;                       // max_batch rounded up to 64 (xs_t: a [groups][64] table per 64 rows)

@@ -427,6 +427,7 @@ int forward_launch(Transformer* t, int batch) {
         p.tp_rank = t->tp_rank;
         p.tp_size = t->tp_size;
         p.err = t->err;
+        p.wait_ns = t->tp_wait_ns;
         return peer_add_quant_launch(p, st, true);
     };
     float* ywo = peer ? slot(0) : t->ybuf;  // where the partial products go
@@ -698,6 +699,10 @@ int tp_join(Transformer* t, int rank, int size, const void* id) {
     if (r != ncclSuccess) return lq_fail(LQ_ECUDA, "NCCL communicator (rank %d of %d): %s", rank, size, f->error_string(r));
     t->comm = comm;
     if (const char* m = getenv("LQ_TP_ALLREDUCE")) t->tp_nccl = strcmp(m, "nccl") == 0;
+    if (const char* w = getenv("LQ_TP_WAIT_MS")) {
+        const long ms = atol(w);
+        if (ms > 0) t->tp_wait_ns = (uint64_t)ms * 1000000ull;
+    }
     return t->tp_nccl ? LQ_OK : xr_setup(t);
 }
 
@@ -984,6 +989,78 @@ int forward_batch_argmax(Transformer* t, const int* tokens, const int* pos, int 
     if (rc) return rc;
     for (int b = 0; b < batch; ++b) next_tokens[b] = t->h_next[b];
     return LQ_OK;
+}
+
+int lq_tp_wait_selftest(int tp_size, int wait_us, double* first_ms, double* second_ms) {
+    if (tp_size < 2 || tp_size > lq::kTpMax || wait_us < 1 || wait_us > 10000000)
+        return lq_fail(LQ_EINVAL, "lq_tp_wait_selftest: tp_size in [2, %d], wait_us in [1, 1e7]", lq::kTpMax);
+    // rank 0 of a tp_size group whose other members never publish: every
+    // process's exchange region lives on this device and only rank 0 runs
+    const int n = 256, gs = 64, ng = n / gs;
+    const size_t region = lq::kXrFlagsBytes + lq::kXrCountersBytes + 2 * (size_t)n * sizeof(float);
+    const size_t bytes = tp_size * region + 4 * (size_t)n * sizeof(float) + n + 2 * ng * 4 + 256;
+    char* buf = nullptr;
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[3] = {};
+    cudaError_t e = cudaMalloc(&buf, bytes);
+    if (e == cudaSuccess) e = cudaMemset(buf, 0, bytes);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking);
+    for (int i = 0; i < 3 && e == cudaSuccess; ++i) e = cudaEventCreate(&ev[i]);
+    int rc = LQ_OK;
+    if (e == cudaSuccess) {
+        char* p = buf + tp_size * region;
+        float* x = reinterpret_cast<float*>(p);
+        float* w = x + n;
+        float* xo = w + n;
+        std::vector<float> ones(n, 1.0f);
+        e = cudaMemcpy(w, ones.data(), n * sizeof(float), cudaMemcpyHostToDevice);
+        PeerAddArgs a{};
+        a.q.mode = IN_ADD_RMSNORM;
+        a.q.n = n;
+        a.q.gs = gs;
+        a.q.nb = 1;
+        a.q.x = x;
+        a.q.rms_w = w;
+        a.q.x_out = xo;
+        a.q.xq = reinterpret_cast<int8_t*>(xo + 2 * n);
+        a.q.xs = reinterpret_cast<float*>(reinterpret_cast<char*>(a.q.xq) + n);
+        a.q.xsum = reinterpret_cast<int*>(a.q.xs + ng);
+        a.err = reinterpret_cast<int*>(a.q.xsum + ng);
+        for (int r = 0; r < tp_size; ++r) {
+            char* base = buf + r * region;
+            a.peer_slot[r] = reinterpret_cast<const float*>(base + lq::kXrFlagsBytes + lq::kXrCountersBytes);
+            a.peer_flag[r] = reinterpret_cast<uint32_t*>(base);  // rank 0's entry of process r's flags
+        }
+        a.my_flags = reinterpret_cast<const uint32_t*>(buf);
+        a.counters = reinterpret_cast<uint32_t*>(buf + lq::kXrFlagsBytes);
+        a.tp_rank = 0;
+        a.tp_size = tp_size;
+        a.wait_ns = (uint64_t)wait_us * 1000ull;
+        if (e == cudaSuccess) e = cudaEventRecord(ev[0], st);
+        if (e == cudaSuccess) e = peer_add_quant_launch(a, st, false);
+        if (e == cudaSuccess) e = cudaEventRecord(ev[1], st);
+        if (e == cudaSuccess) e = peer_add_quant_launch(a, st, false);  // the step's next call: no second wait
+        if (e == cudaSuccess) e = cudaEventRecord(ev[2], st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        float t1 = 0.0f, t2 = 0.0f;
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&t1, ev[0], ev[1]);
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&t2, ev[1], ev[2]);
+        if (first_ms) *first_ms = t1;
+        if (second_ms) *second_ms = t2;
+        if (e == cudaSuccess) {
+            int h = 0;
+            e = cudaMemcpy(&h, a.err, sizeof(int), cudaMemcpyDeviceToHost);
+            if (e == cudaSuccess)
+                rc = h ? lq_fail(LQ_ETIMEOUT, "device-side wait gave up (code 0x%x)", h)
+                       : lq_fail(LQ_EINVAL, "lq_tp_wait_selftest: the wait did not give up");
+        }
+    }
+    if (e != cudaSuccess) rc = cuda_fail(e, "lq_tp_wait_selftest");
+    for (cudaEvent_t x : ev)
+        if (x) cudaEventDestroy(x);
+    if (st) cudaStreamDestroy(st);
+    if (buf) cudaFree(buf);
+    return rc;
 }
 
 int transformer_config(const Transformer* t, Config* cfg, int* kind, int* group_size) {

@@ -20,6 +20,8 @@
 //  * The first call on each device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
 //    before any stream capture.
+//  * A device-side wait that gives up inside one of these calls sets the
+//    array's error word; lq_sync reports it (LQ_ETIMEOUT) and clears it.
 #include <cstdint>
 #include <cstdio>
 
@@ -86,9 +88,23 @@ extern "C" int matmul_f32_noalloc(float* xout, const float* x, const QuantizedTe
     int* xsum = reinterpret_cast<int*>(base + kXqBytes + kGroupBytes);
     int* err = reinterpret_cast<int*>(base + kErrOff);
     cudaStream_t st = lq::stream();
-    // the error word must start at zero; the activation, scales and sums are
-    // fully rewritten by the quantizer before the GEMV reads them
-    e = cudaMemsetAsync(err, 0, sizeof(int), st);
-    if (e != cudaSuccess) return lq::cuda_fail(e, "matmul_f32_noalloc: clear error word");
+    // The activation, scales and sums are fully rewritten by the quantizer
+    // before the GEMV reads them.  The error word starts at zero (static
+    // device memory is zero-initialised) and goes back to zero whenever
+    // lq_sync reports it, so a device-side error of any call stays recorded
+    // until the next lq_sync.
     return lq::matmul_f32_device(xout, x, w, n, d, xq, xs, xsum, err, st, false, num_sms, nullptr);
 }
+
+namespace lq {
+
+// Report (and clear) the error word of the fixed scratch on the current
+// device, if matmul_f32_noalloc has been used there.  Called by lq_sync.
+int noalloc_check_error(cudaStream_t st) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || !g_noalloc_addr[dev]) return LQ_OK;
+    int* err = reinterpret_cast<int*>(static_cast<unsigned char*>(g_noalloc_addr[dev]) + kErrOff);
+    return check_device_error(err, st);
+}
+
+}  // namespace lq

@@ -170,6 +170,7 @@ struct OrcModel {
     OrcConfig c;
     int kind, gs;
     int mma_grid; /* > 0: GEMVs in the tensor-core GEMM's order for this grid size */
+    int tp;       /* > 1: the tensor-parallel step over tp processes (wo / w2 as per-process column slices) */
     float *emb, *rms_att, *rms_ffn, *rms_final;
     OrcQ wq, wk, wv, wo, w1, w2, w3, wcls;
     uint8_t* file;      /* whole file in memory */
@@ -180,7 +181,44 @@ struct OrcModel {
     float *x, *xb, *xb2, *hb, *hb2, *q, *att, *logits, *kc, *vc;
     int8_t* aq;
     float* as;
+    /* optional trace of every int8 activation the forwards compute, in order */
+    int8_t* trace;
+    long trace_cap, trace_n;
+    /* optional override: the next forward uses these int8 activations and
+     * group scales in place of its own, value by value in call order */
+    const int8_t* ovr_q;
+    const float* ovr_s;
+    long ovr_cap, ovr_n;
 };
+
+static void act_trace(OrcModel* m, int n) {
+    if (m->ovr_q && m->ovr_n + n <= m->ovr_cap) {
+        memcpy(m->aq, m->ovr_q + m->ovr_n, (size_t)n);
+        memcpy(m->as, m->ovr_s + m->ovr_n / m->gs, (size_t)(n / m->gs) * sizeof(float));
+    }
+    m->ovr_n += n;
+    for (int i = 0; i < n; i++) {
+        if (m->trace && m->trace_n < m->trace_cap) m->trace[m->trace_n] = m->aq[i];
+        m->trace_n++;
+    }
+}
+
+long orc_act_override(OrcModel* m, const int8_t* xq, const float* xs, long n) {
+    long used = m->ovr_n;
+    m->ovr_q = xq;
+    m->ovr_s = xs;
+    m->ovr_cap = n;
+    m->ovr_n = 0;
+    return used;
+}
+
+long orc_act_trace(OrcModel* m, int8_t* buf, long cap) {
+    long n = m->trace_n;
+    m->trace = buf;
+    m->trace_cap = cap;
+    m->trace_n = 0;
+    return n;
+}
 
 static int take(uint8_t** p, uint8_t* end, size_t n, void** out) {
     if ((size_t)(end - *p) < n) return -1;
@@ -336,6 +374,7 @@ float* orc_forward(OrcModel* m, int token, int pos) {
         float* k = m->kc + loff + (size_t)pos * kv_dim;
         float* v = m->vc + loff + (size_t)pos * kv_dim;
         orc_quantize_act(m->xb, dim, gs, m->aq, m->as, NULL);     /* :345 */
+        act_trace(m, dim);
         qmatmul(m, m->q, &m->wq, l, dim, dim);                     /* :346-348 */
         qmatmul(m, k, &m->wk, l, kv_dim, dim);
         qmatmul(m, v, &m->wv, l, kv_dim, dim);
@@ -371,10 +410,12 @@ float* orc_forward(OrcModel* m, int token, int pos) {
             }
         }
         orc_quantize_act(m->xb, dim, gs, m->aq, m->as, NULL);     /* :394-396 */
+        act_trace(m, dim);
         qmatmul(m, m->xb2, &m->wo, l, dim, dim);
         for (int i = 0; i < dim; i++) x[i] += m->xb2[i];
         rmsnorm(m->xb, x, m->rms_ffn + l * dim, dim);              /* :399-402 */
         orc_quantize_act(m->xb, dim, gs, m->aq, m->as, NULL);
+        act_trace(m, dim);
         qmatmul(m, m->hb, &m->w1, l, hidden, dim);
         qmatmul(m, m->hb2, &m->w3, l, hidden, dim);
         for (int i = 0; i < hidden; i++) {                         /* SwiGLU :405-410 */
@@ -384,11 +425,13 @@ float* orc_forward(OrcModel* m, int token, int pos) {
             m->hb[i] = val;
         }
         orc_quantize_act(m->hb, hidden, gs, m->aq, m->as, NULL);  /* :412-414 */
+        act_trace(m, hidden);
         qmatmul(m, m->xb, &m->w2, l, dim, hidden);
         for (int i = 0; i < dim; i++) x[i] += m->xb[i];
     }
     rmsnorm(x, x, m->rms_final, dim);                              /* :417-419 */
     orc_quantize_act(x, dim, gs, m->aq, m->as, NULL);
+    act_trace(m, dim);
     orc_gemv(m->logits, m->aq, m->as, m->wcls.q, m->wcls.s, p->vocab_size, dim, gs, m->kind);
     return m->logits;
 }
@@ -598,6 +641,29 @@ static void mirror_gemv(float* out, const OrcQ* w, int64_t l, int64_t rows, cons
     for (int64_t r = 0; r < rows; r++) out[r] = mirror_row(q + r * rb, s + r * (n / gs), xq, xs, n, gs, kind, o, r);
 }
 
+/* Tensor parallelism: a row-parallel product (wo, w2) as tp partial products
+ * over consecutive column slices (each in the GEMV's order for its slice
+ * length), summed in process order: ((y_0 + y_1) + y_2) + ... */
+static void mirror_gemv_tp(float* out, const OrcQ* w, int64_t l, int64_t rows, const int8_t* xq, const float* xs, int n,
+                           int gs, int kind, int tp) {
+    int ns = n / tp, ng = n / gs, ngs = ns / gs;
+    size_t rb = row_bytes(n, kind), rbs = row_bytes(ns, kind);
+    RowOrder o = row_order(ns, gs, kind, 0, rows % 2 == 0);
+    const uint8_t* q = w->q + (size_t)l * rows * rb;
+    const float* s = w->s + (size_t)l * rows * ng;
+    for (int64_t r = 0; r < rows; r++) {
+        float y = 0.0f;
+        for (int p = 0; p < tp; p++) {
+            float v = mirror_row(q + r * rb + p * rbs, s + r * ng + p * ngs, xq + (size_t)p * ns, xs + (size_t)p * ngs,
+                                 ns, gs, kind, o, r);
+            y = p == 0 ? v : y + v;
+        }
+        out[r] = y;
+    }
+}
+
+void orc_set_tp(OrcModel* m, int tp) { m->tp = tp; }
+
 /* attention of one head over positions 0..pos in chunks of 64 (kernel order) */
 static void mirror_attention(const float* q, const float* kc, const float* vc, size_t stride, int pos, int hs,
                              float* out) {
@@ -688,6 +754,7 @@ float* orc_forward_kernel_order(OrcModel* m, int token, int pos) {
         float* k = m->kc + loff + (size_t)pos * kv_dim;
         float* v = m->vc + loff + (size_t)pos * kv_dim;
         mirror_act_quant(x, m->rms_att + l * dim, dim, gs, m->aq, m->as, tmp);    /* runq.c:338,345 */
+        act_trace(m, dim);
         mirror_gemv(m->q, &m->wq, l, dim, m->aq, m->as, dim, gs, kind, o_q);        /* :346-348 */
         mirror_gemv(k, &m->wk, l, kv_dim, m->aq, m->as, dim, gs, kind, o_k);
         mirror_gemv(v, &m->wv, l, kv_dim, m->aq, m->as, dim, gs, kind, o_v);
@@ -708,9 +775,14 @@ float* orc_forward_kernel_order(OrcModel* m, int token, int pos) {
             mirror_attention(m->q + h * hs, m->kc + loff + (h / kv_mul) * hs, m->vc + loff + (h / kv_mul) * hs,
                              (size_t)kv_dim, pos, hs, m->xb + h * hs);
         mirror_act_quant(m->xb, NULL, dim, gs, m->aq, m->as, tmp);                   /* :394-396 */
-        mirror_gemv(m->xb2, &m->wo, l, dim, m->aq, m->as, dim, gs, kind, o_wo);
+        act_trace(m, dim);
+        if (m->tp > 1)
+            mirror_gemv_tp(m->xb2, &m->wo, l, dim, m->aq, m->as, dim, gs, kind, m->tp);
+        else
+            mirror_gemv(m->xb2, &m->wo, l, dim, m->aq, m->as, dim, gs, kind, o_wo);
         for (int i = 0; i < dim; i++) x[i] += m->xb2[i];
         mirror_act_quant(x, m->rms_ffn + l * dim, dim, gs, m->aq, m->as, tmp);      /* :399-402 */
+        act_trace(m, dim);
         mirror_gemv(m->hb, &m->w1, l, hidden, m->aq, m->as, dim, gs, kind, o_ffn);
         mirror_gemv(m->hb2, &m->w3, l, hidden, m->aq, m->as, dim, gs, kind, o_ffn);
         for (int i = 0; i < hidden; i++) {                                           /* SwiGLU :405-410 */
@@ -719,10 +791,15 @@ float* orc_forward_kernel_order(OrcModel* m, int token, int pos) {
             m->hb[i] = val * m->hb2[i];
         }
         mirror_act_quant(m->hb, NULL, hidden, gs, m->aq, m->as, tmp);                /* :412-414 */
-        mirror_gemv(m->xb, &m->w2, l, dim, m->aq, m->as, hidden, gs, kind, o_w2);
+        act_trace(m, hidden);
+        if (m->tp > 1)
+            mirror_gemv_tp(m->xb, &m->w2, l, dim, m->aq, m->as, hidden, gs, kind, m->tp);
+        else
+            mirror_gemv(m->xb, &m->w2, l, dim, m->aq, m->as, hidden, gs, kind, o_w2);
         for (int i = 0; i < dim; i++) x[i] += m->xb[i];
     }
     mirror_act_quant(x, m->rms_final, dim, gs, m->aq, m->as, tmp);                   /* :417-419 */
+    act_trace(m, dim);
     mirror_gemv(m->logits, &m->wcls, 0, p->vocab_size, m->aq, m->as, dim, gs, kind, o_cls);
     free(tmp);
     return m->logits;

@@ -73,10 +73,24 @@ float* orc_forward_kernel_order(OrcModel* m, int token, int pos);
 /* grid > 0: orc_forward_kernel_order mirrors the batched step, whose products
  * run on the tensor-core GEMM with `grid` CTAs (stream-K order); 0: batch-1 GEMV */
 void orc_set_mma_grid(OrcModel* m, int grid);
+/* tp > 1: orc_forward_kernel_order mirrors the tensor-parallel batch-1 step
+ * over tp processes: wo and w2 as tp partial products over consecutive
+ * column slices, summed in process order (the peer all-reduce's order) */
+void orc_set_tp(OrcModel* m, int tp);
 /* the tensor-core GEMM's fp32 order for one matrix of a launch: rows of tiles
  * tile0.. of a launch of `tiles` 128-row tiles over `grid` CTAs */
 void orc_gemm_mma(float* out, const int8_t* xq, const float* xs, const uint8_t* wq, const float* ws, int B,
                   int64_t rows, int64_t n, int gs, int kind, int tile0, int tiles, int grid);
+/* Record every int8 activation value the next forwards compute (in call
+ * order: attention input, attention output, ffn input, ffn hidden per layer,
+ * then the final norm) into buf, up to cap values; NULL stops.  Returns the
+ * number of values computed since the previous call. */
+long orc_act_trace(OrcModel* m, int8_t* buf, long cap);
+/* Make the next forwards use the given int8 activations (n values, in the
+ * trace's call order) and their group scales (n / gs values) in place of
+ * their own quantizer outputs; NULL turns it off.  Returns the number of
+ * values consumed since the previous call. */
+long orc_act_override(OrcModel* m, const int8_t* xq, const float* xs, long n);
 /* exp as evaluated by the product (Cody-Waite + Taylor degree 7). */
 float orc_expf(float x);
 /* sample_argmax, runq.c:578-585: first index of the maximum. */

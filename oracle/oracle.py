@@ -48,8 +48,13 @@ def orc() -> C.CDLL:
         L.orc_forward_kernel_order.argtypes = [_P, I, I]
         L.orc_gemm_mma.argtypes = [_P, _P, _P, _P, _P, I, I64, I64, I, I, I, I, I]
         L.orc_set_mma_grid.argtypes = [_P, I]
+        L.orc_set_tp.argtypes = [_P, I]
         L.orc_expf.restype = C.c_float
         L.orc_expf.argtypes = [C.c_float]
+        L.orc_act_trace.restype = C.c_long
+        L.orc_act_trace.argtypes = [_P, _P, C.c_long]
+        L.orc_act_override.restype = C.c_long
+        L.orc_act_override.argtypes = [_P, _P, _P, C.c_long]
         _orc = L
     return _orc
 
@@ -72,8 +77,16 @@ def ref() -> C.CDLL:
         L.ref_vocab.argtypes = [_P]
         L.ref_free.argtypes = [_P]
         L.ref_set_threads.argtypes = [I]
+        L.ref_act_trace.restype = C.c_long
+        L.ref_act_trace.argtypes = [_P, _P, C.c_long]
         _ref = L
     return _ref
+
+
+def _act_values(config) -> int:
+    """int8 activation values one decode step quantizes (runq.c:345,394,400,412,418)."""
+    dim, hidden, layers = config[0], config[1], config[2]
+    return layers * (3 * dim + hidden) + dim
 
 
 # ---- oracle wrappers -----------------------------------------------------------
@@ -158,10 +171,40 @@ class OracleModel:
         the tensor-core GEMM with `grid` CTAs); 0: the batch-1 GEMV."""
         orc().orc_set_mma_grid(self.h, grid)
 
+    def set_tp(self, tp: int) -> None:
+        """tp > 1: forward_kernel_order mirrors the tensor-parallel batch-1
+        step over tp processes (wo / w2 partials summed in process order)."""
+        orc().orc_set_tp(self.h, tp)
+
     def forward_kernel_order(self, token: int, pos: int) -> np.ndarray:
         """The step in the product kernels' fp32 reduction order."""
         p = orc().orc_forward_kernel_order(self.h, token, pos)
         return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def forward_kernel_order_traced(self, token: int, pos: int):
+        """forward_kernel_order plus every int8 activation value of the step,
+        in call order (attention input, attention output, ffn input, ffn
+        hidden per layer, then the final norm)."""
+        buf = np.empty(_act_values(self.config), np.int8)
+        orc().orc_act_trace(self.h, _ptr(buf), buf.size)
+        lg = self.forward_kernel_order(token, pos)
+        n = orc().orc_act_trace(self.h, None, 0)
+        assert n == buf.size, (n, buf.size)
+        return lg, buf
+
+    def forward_kernel_order_with(self, token: int, pos: int, xq: np.ndarray, xs: np.ndarray) -> np.ndarray:
+        """forward_kernel_order with every int8 activation and group scale of
+        the step replaced by the given ones (e.g. runq.c's, from
+        RefRunq.forward_traced): isolates the fp32 summation order from int8
+        rounding flips."""
+        xq = np.ascontiguousarray(xq, np.int8)
+        xs = np.ascontiguousarray(xs, np.float32)
+        assert xq.size == _act_values(self.config) and xs.size == xq.size // self.gs
+        orc().orc_act_override(self.h, _ptr(xq), _ptr(xs), xq.size)
+        lg = self.forward_kernel_order(token, pos)
+        n = orc().orc_act_override(self.h, None, None, 0)
+        assert n == xq.size, (n, xq.size)
+        return lg
 
     def close(self):
         if self.h:
@@ -182,6 +225,23 @@ class RefRunq:
     def forward(self, token: int, pos: int) -> np.ndarray:
         p = ref().ref_forward(self.h, token, pos)
         return np.ctypeslib.as_array(p, shape=(self.vocab,)).copy()
+
+    def forward_traced(self, token: int, pos: int, config):
+        """forward plus the int8 activations quantize_act produced in the step
+        and their group scales (recorded through the shim's fabsf / lrintf
+        wrappers), in call order: (logits, xq [values], xs [values / 32])."""
+        nv = _act_values(config)
+        q = np.empty(nv, np.int8)
+        ax = np.empty(nv, np.float32)
+        ref().ref_act_trace(_ptr(q), _ptr(ax), nv)
+        lg = self.forward(token, pos)
+        n = ref().ref_act_trace(None, None, 0)
+        assert n == nv, (n, nv)
+        # quantize_act's group scale (runq.c:126-127), float32 arithmetic
+        amax = ax.reshape(-1, 32).max(axis=1)
+        xs = (amax / np.float32(127.0)).astype(np.float32)
+        xs[xs == 0] = np.float32(1e-8)
+        return lg, q, xs
 
     def close(self):
         if self.h:

@@ -8,13 +8,55 @@
  *   quantize_act  runq.c:117-139
  *   matmul_q8     runq.c:142-159
  *   build_transformer / forward / free_transformer  runq.c:280-421
- * and bench.py --impl reference can time it on the host cores.
+ * plus a trace of the int8 activations forward() computes (for locating the
+ * first position where a different fp32 summation order changes one int8
+ * value), and bench.py --impl reference can time it on the host cores.
  */
+#include <math.h>
+#include <stdint.h>
+
+/* Activation trace: runq.c calls fabsf and lrintf only inside quantize_act
+ * (runq.c:123 and :130), each once per value in order, so wrapping them
+ * records every activation quantize_act sees (|x|, from which the group
+ * scale amax/127 follows) and every int8 value it produces (clamped as
+ * quantize_act clamps it), without touching the reference source.  Off
+ * unless buffers are set. */
+static int8_t* g_act_q;
+static float* g_act_abs;
+static long g_act_cap, g_act_nq, g_act_nabs;
+
+static long ref_lrintf_traced(float v) {
+    long q = lrintf(v);
+    if (g_act_q && g_act_nq < g_act_cap) g_act_q[g_act_nq] = (int8_t)(q > 127 ? 127 : (q < -127 ? -127 : q));
+    g_act_nq++;
+    return q;
+}
+
+static float ref_fabsf_traced(float v) {
+    float a = fabsf(v);
+    if (g_act_abs && g_act_nabs < g_act_cap) g_act_abs[g_act_nabs] = a;
+    g_act_nabs++;
+    return a;
+}
+#define lrintf(v) ref_lrintf_traced(v)
+#define fabsf(v) ref_fabsf_traced(v)
+
 #define main runq_main
 #include "v1-int8-vnni/runq.c"
 #undef main
+#undef lrintf
+#undef fabsf
 
-#include <omp.h>
+/* Start recording into q (int8 values) and absx (|x|), cap values each (NULL
+ * stops); returns the number of values quantized since the previous call. */
+long ref_act_trace(int8_t* q, float* absx, long cap) {
+    long n = g_act_nq;
+    g_act_q = q;
+    g_act_abs = absx;
+    g_act_cap = cap;
+    g_act_nq = g_act_nabs = 0;
+    return n;
+}
 
 void ref_quantize_act(const float* x, int n, int8_t* xq, float* xs, float* xt) {
     quantize_act(x, n, xq, xs, xt);

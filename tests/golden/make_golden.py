@@ -9,8 +9,13 @@ against outputs of the reference code itself, produced here:
     read out through one-group rows), and build_transformer/forward on the
     tiny config-1 checkpoint;
   * the runq binary's stdout on that checkpoint with a synthetic tokenizer.
+  * runq.c's greedy streams on config-1 checkpoints of three seeds, with the
+    position of the first int8 activation that differs from the kernel-order
+    oracle's (the product's arithmetic) and the largest relative logits
+    difference seen when the oracle is fed runq.c's own int8 activations.
 Usage (needs the reference tree, so it runs only on the build machine):
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
+(or set LLAMA2Q_REF to the reference project root).
 """
 from __future__ import annotations
 
@@ -31,10 +36,12 @@ sys.path.insert(0, os.path.join(ROOT, "tests"))
 
 import oracle as O  # noqa: E402
 import synth  # noqa: E402
+from runq_parity import flip_survey  # noqa: E402
 
 TINY = synth.TINY_CONFIG
 TINY_SEED = synth.TINY_SEED
 LOGIT_POSITIONS = (0, 1, 2, 16, 63, 255)
+FLIP_SEEDS = (1234, 42, 7)
 
 
 def main(ref_root: str) -> None:
@@ -125,8 +132,34 @@ def main(ref_root: str) -> None:
                         seed=np.array(TINY_SEED, np.uint64), sha256_q8=np.array(sha8), sha256_q4=np.array(sha4),
                         stream=np.array(stream, np.int32), gaps=np.array(gaps, np.float32),
                         stdout=np.frombuffer(out, np.uint8), **logits)
+
+    # 4. int8 flip survey over three seeds (the checkpoint bytes are pinned to
+    #    tools/quantize_int8.py's output for each seed)
+    flips = {}
+    with tempfile.TemporaryDirectory() as d:
+        for seed in FLIP_SEEDS:
+            f32 = os.path.join(d, f"f32_{seed}.bin")
+            ref8 = os.path.join(d, f"q8_{seed}.bin")
+            lq.write_checkpoint_fp32(f32, lq.Config.make(*TINY), seed, 0.02, False)
+            subprocess.run([sys.executable, os.path.join(ref_root, "tools", "quantize_int8.py"), f32, ref8],
+                           check=True, capture_output=True)
+            ours = synth.tiny_checkpoint(8, 32, seed=seed)
+            assert open(ours, "rb").read() == open(ref8, "rb").read(), seed
+            f = flip_survey(ref8, TINY[6])
+            stream, first, before, corrected = f["stream"], f["first_flip"], f["rel_before"], f["rel_corrected"]
+            flips[f"stream_{seed}"] = stream
+            flips[f"first_flip_{seed}"] = np.array(first, np.int32)
+            flips[f"rel_before_{seed}"] = np.array(before, np.float64)
+            flips[f"rel_corrected_{seed}"] = np.array(corrected, np.float64)
+            flips[f"sha256_{seed}"] = np.array(hashlib.sha256(open(ref8, "rb").read()).hexdigest())
+            print(f"seed {seed}: first int8 flip at position {first}, max rel before {before:.2e}, "
+                  f"flip-corrected max rel over {TINY[6]} positions {corrected:.2e}")
+    np.savez_compressed(os.path.join(HERE, "runq_flips.npz"), seeds=np.array(FLIP_SEEDS, np.int64), **flips)
     print("golden fixtures written to", HERE)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LLAMA2Q_REF")
+    if not ref:
+        sys.exit("usage: make_golden.py /path/to/reference (or set LLAMA2Q_REF)")
+    main(ref)

@@ -22,6 +22,12 @@ TINY_SEED = 1234
 # group-size-64 and GQA coverage at a small shape: dim 256, hidden 768,
 # 4 layers, 4 query heads / 2 kv heads (head 64), vocab 4096, seq 128
 SMALL64_CONFIG = (256, 768, 4, 4, 2, 4096, 128)
+# head size 128 (the 7B / 13B / 70B head), multi-head: dim 256, 2 heads, 2
+# layers, long context (seq 1280) for the split-KV merge over 18+ chunks
+HEAD128_CONFIG = (256, 768, 2, 2, 2, 512, 1280)
+# head size 128 with 8:1 grouped-query attention (the 70B layout, one kv head
+# serving 8 query heads): dim 1024, 1 layer, seq 1280
+GQA8_CONFIG = (1024, 1024, 1, 8, 1, 512, 1280)
 
 
 def lq():
