@@ -182,6 +182,89 @@ def cpu_baseline(seconds: float = 10.0, steps: int | None = None, warmup: int = 
     return gbs, kind, cores, desc + f"; {len(times)} passes", times
 
 
+def cpu_model() -> str:
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def _run_timed(cmd, env):
+    """Run a reference runner; (achieved tok/s from its own stderr line, wall s)."""
+    import re
+
+    t0 = time.perf_counter()
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=900)
+    wall = time.perf_counter() - t0
+    m = re.search(r"achieved tok/s: ([0-9.]+)", r.stderr)
+    if r.returncode != 0 or not m:
+        return None, wall, (r.stderr or r.stdout)[-300:]
+    return float(m.group(1)), wall, None
+
+
+def cpu_decode_baselines(with_7b: bool):
+    """The reference's CPU runners end to end, on this host's cores, each with
+    its own `achieved tok/s` line (v1-int8-vnni/runq.c:710-716,
+    v0-fp32/run.c:776-779, which leave out the first token), built from the
+    reference sources into oracle/_ref:
+      * runq.c (INT8 GS32, AVX-512 VNNI + OpenMP) on the config-1 checkpoint,
+        greedy from BOS, 256 steps;
+      * run.c (fp32 + OpenMP) on the same model's fp32 export;
+      * runq.c on a Llama-2-7B-shape INT8 GS32 file (7.96 GB, written here
+        with seeded weights), 32 steps — with_7b only, when host memory allows.
+    Seeded synthetic models (no public checkpoint is involved)."""
+    import tempfile
+
+    ref_dir = os.path.join(ROOT, "oracle", "_ref")
+    runq, run32 = os.path.join(ref_dir, "runq"), os.path.join(ref_dir, "run_fp32")
+    cores = os.cpu_count() or 1
+    out = {"cores": cores, "cpu": cpu_model(), "threads": "OMP_NUM_THREADS=%d" % cores,
+           "kind": "reference", "timing": "each runner's own achieved tok/s line (first token excluded)"}
+    if not (os.access(runq, os.X_OK) and os.access(run32, os.X_OK)):
+        out["unavailable"] = "oracle/_ref runners not built (reference sources absent at build time)"
+        return out
+    if not cpu_has_vnni():
+        out["unavailable"] = "host CPU lacks AVX-512 VNNI, which runq.c needs"
+        return out
+    sys.path.insert(0, os.path.join(ROOT, "tests"))
+    import synth
+
+    lq = importlib.import_module("llama2-min-inference_b200")
+    env = dict(os.environ, OMP_NUM_THREADS=str(cores))
+    with tempfile.TemporaryDirectory() as d:
+        cfg = lq.Config.make(*synth.TINY_CONFIG)
+        f32, q8, tok = os.path.join(d, "c1_f32.bin"), os.path.join(d, "c1_q8.bin"), os.path.join(d, "tok.bin")
+        lq.write_checkpoint_fp32(f32, cfg, synth.TINY_SEED, 0.02, False)
+        lq.quantize_checkpoint(f32, q8, lq.KIND_INT8, 32)
+        synth.write_tokenizer(tok, cfg.vocab_size)
+        for name, cmd in (("runq_config1_int8_gs32", [runq, q8]), ("run_fp32_config1", [run32, f32])):
+            v, wall, err = _run_timed(cmd + ["-z", tok, "-t", "0", "-n", "256", "-s", "1"], env)
+            out[name] = {"tok_s": v, "wall_s": round(wall, 3), "steps": 256} if v else {"error": err}
+        if with_7b:
+            try:
+                mem = os.sysconf("SC_PAGE_SIZE") * os.sysconf("SC_AVPHYS_PAGES")
+            except (ValueError, OSError):
+                mem = 0
+            c7 = lq.Config.make(4096, 11008, 32, 32, 32, 32000, 2048)
+            if mem < 24 * 2**30:
+                out["runq_7b_int8_gs32"] = {"unavailable": "less than 24 GB of free host memory"}
+            else:
+                p7 = os.path.join(d, "7b_q8.bin")
+                t0 = time.perf_counter()
+                lq.write_checkpoint_random(p7, c7, lq.KIND_INT8, 32, 7, 0.02)
+                gen = time.perf_counter() - t0
+                lq_tok = os.path.join(d, "tok7.bin")
+                synth.write_tokenizer(lq_tok, 32000)
+                v, wall, err = _run_timed([runq, p7, "-z", lq_tok, "-t", "0", "-n", "32", "-s", "1"], env)
+                out["runq_7b_int8_gs32"] = ({"tok_s": v, "wall_s": round(wall, 2), "steps": 32,
+                                             "file_bytes": os.path.getsize(p7), "file_write_s": round(gen, 1)}
+                                            if v else {"error": err})
+    return out
+
+
 # ---------------------------------------------------------------------------
 
 def setup_dist(n_gpus: int):
@@ -194,7 +277,7 @@ def setup_dist(n_gpus: int):
 
         import torch.distributed as dist
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
     return rank, world, local, dist
 
 
@@ -206,17 +289,62 @@ def run_reference(args):
         return
     gbs, kind, cores, desc, times = cpu_baseline(steps=args.steps, warmup=args.warmup)
     ms = 1e3 * sum(times) / len(times)
+    try:
+        decode = cpu_decode_baselines(with_7b=not args.no_decode)
+    except Exception as e:  # reported, never hides the GEMV line
+        decode = {"error": str(e)[:300]}
     line = {"metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "u8/s8 (int32 group dot, fp32 scales)", "data": "synthetic",
             "impl": "reference",
             "config": {"workload": WORKLOAD, "group_size_reference": 32,
                        "note": "reference runq.c supports only group size 32 (QBLOCK, runq.c:26)"},
-            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc},
-            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc,
+                             "cpu": cpu_model()},
+            "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "reference_decode_cpu": decode}
     print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
+
+
+def step_breakdown(lq, t, tokens, pos):
+    """One traced decode step (device clock stamps of every kernel, see
+    transformer_trace): the step's device time and, per kernel kind, the
+    launch count, the time on the step's critical path (end of the kernel
+    minus end of the one before it, in launch order) and the time from its
+    dependency release to its end.  Tracing is switched off again after."""
+    import numpy as np
+
+    t.trace(True)
+    B = len(tokens)
+    for _ in range(2):  # the first step captures the traced graph
+        t.forward_batch_argmax(np.asarray(tokens, np.int32), np.full(B, pos, np.int32))
+    kinds, st = t.trace_read()
+    t.trace(False)
+    valid = (st < np.uint64(1) << np.uint64(63)).all(1)
+    out = {"kernels": int(len(kinds))}
+    if not valid.any():
+        return out
+    st = st.astype(np.float64)
+    t0 = st[valid, 0].min()
+    t_end = st[valid, 2].max()
+    out["step_us"] = round((t_end - t0) / 1e3, 2)
+    by = {}
+    prev_end = t0
+    for i, k in enumerate(kinds):
+        name = lq.TRACE_KINDS.get(int(k), str(k))
+        d = by.setdefault(name, {"count": 0, "critical_us": 0.0, "busy_us": 0.0})
+        d["count"] += 1
+        if valid[i]:
+            d["critical_us"] += max(0.0, st[i, 2] - prev_end) / 1e3
+            d["busy_us"] += max(0.0, st[i, 2] - st[i, 1]) / 1e3
+            prev_end = max(prev_end, st[i, 2])
+    for d in by.values():
+        d["critical_us"] = round(d["critical_us"], 2)
+        d["busy_us"] = round(d["busy_us"], 2)
+    out["by_kind"] = by
+    return out
 
 
 def decode_bench(lq, torch, positions: int = 2048):
@@ -235,6 +363,7 @@ def decode_bench(lq, torch, positions: int = 2048):
     for pos in range(positions):
         token = t.forward_argmax(token, pos)
     dt = time.perf_counter() - t0
+    breakdown = step_breakdown(lq, t, [token], positions - 1)
     t.close()
     wbytes = (4096 * 4096 * 4 + 4096 * 11008 * 3) * 32 + 32000 * 4096
     wbytes = wbytes // 2 + wbytes // 64 * 4
@@ -244,7 +373,8 @@ def decode_bench(lq, torch, positions: int = 2048):
             "weight_bytes_per_token": wbytes, "avg_kv_bytes_per_token": int(kv_avg),
             "hbm_gbs_effective": round((wbytes + kv_avg) * positions / dt / 1e9, 1),
             "timing": "host wall clock around forward_argmax calls (H2D token/pos, graph, D2H 4 bytes each)",
-            "init_s": round(init_s, 2)}
+            "init_s": round(init_s, 2),
+            "step_breakdown_last_position": breakdown}
 
 
 def batch_bench(lq, torch, batches=(1, 8, 16, 32, 64), ctx: int = 1024, steps: int = 8):
@@ -296,6 +426,69 @@ def batch_bench(lq, torch, batches=(1, 8, 16, 32, 64), ctx: int = 1024, steps: i
     return out
 
 
+def _group_id(lq, torch, rank, world, dist):
+    if world == 1:
+        return None
+    buf = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        buf.copy_(torch.frombuffer(bytearray(lq.tp_unique_id()), dtype=torch.uint8))
+    dist.broadcast(buf, 0)
+    return bytes(buf.cpu().numpy().tobytes())
+
+
+def tp_check(lq, torch, rank, world, dist, layers: int = 2, tokens=(1, 3000, 17, 9)):
+    """Correctness of the tensor-parallel step inside the benchmark run: the
+    70B layer shape with `layers` layers, 4 teacher-forced positions, on every
+    process with the peer all-reduce and with NCCL; rank 0 also runs the
+    unsplit model on its GPU.  Reports whether every process returned the
+    same logits, whether the peer and NCCL all-reduces agree bit for bit
+    (they must with 2 processes, where both sums are y_0 + y_1; with more,
+    NCCL may associate the sum differently) and the largest relative logits
+    difference against the one-GPU model (the split only re-associates the
+    wo / w2 sums, so the difference is fp32 rounding until an int8
+    activation flips)."""
+    cfg = lq.Config.make(8192, 28672, layers, 64, 8, 32000, 64)
+    outs = {}
+    for mode in ("peer", "nccl"):
+        if mode == "nccl" and world == 1:
+            break
+        gid = _group_id(lq, torch, rank, world, dist)
+        if mode == "nccl":
+            os.environ["LQ_TP_ALLREDUCE"] = "nccl"
+        try:
+            t = lq.Transformer.random_tp(cfg, lq.KIND_INT4, 64, 29, rank, world, gid, 64)
+        finally:
+            os.environ.pop("LQ_TP_ALLREDUCE", None)
+        outs[mode] = np.stack([t.forward(tok, pos).copy() for pos, tok in enumerate(tokens)])
+        t.close()
+    res = {"layers": layers, "positions": len(tokens)}
+    mine = torch.from_numpy(outs["peer"]).cuda()
+    if dist:
+        allp = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allp, mine)
+        res["all_ranks_identical"] = all(bool(torch.equal(allp[0], x)) for x in allp)
+    else:
+        res["all_ranks_identical"] = True
+    if "nccl" in outs:
+        a, b = outs["peer"], outs["nccl"]
+        eq = torch.tensor([int(np.array_equal(a.view(np.uint32), b.view(np.uint32)))], device="cuda")
+        if dist:
+            dist.all_reduce(eq, op=dist.ReduceOp.MIN)
+        res["peer_equals_nccl"] = bool(eq.item())
+        res["peer_vs_nccl_max_rel"] = float(np.abs(a - b).max() / np.abs(b).max())
+    if rank == 0:
+        ref = lq.Transformer.random(cfg, lq.KIND_INT4, 64, 29, 64)
+        want = np.stack([ref.forward(tok, pos).copy() for pos, tok in enumerate(tokens)])
+        ref.close()
+        a = outs["peer"]
+        res["max_rel_vs_1gpu"] = float(np.abs(a - want).max() / np.abs(want).max())
+        res["argmax_agree_vs_1gpu"] = float(np.mean(np.argmax(a, -1) == np.argmax(want, -1)))
+        res["bitwise_equal_1gpu"] = bool(np.array_equal(a.view(np.uint32), want.view(np.uint32)))
+    if dist:
+        dist.barrier()
+    return res
+
+
 def tp_bench(lq, torch, rank, world, dist, ctx: int = 2048, steps1: int = 16, steps16: int = 8):
     """Config 5: Llama-2-70B-shape INT4 GS64 decode, tensor-parallel over the
     job's GPUs (one process per GPU), batch 1 and batch 16 at context ctx
@@ -304,29 +497,27 @@ def tp_bench(lq, torch, rank, world, dist, ctx: int = 2048, steps1: int = 16, st
     memory (NVLink); with more than one GPU the NCCL all-reduce
     (LQ_TP_ALLREDUCE=nccl) is timed too, as the baseline.  Every process runs
     the same steps; the time is the slowest process's wall clock around the
-    timed steps."""
+    timed steps.  With more than one GPU, rank 0 first times the same model on
+    its GPU alone, for the speed-up and efficiency of the split."""
     D, H, L, V = 8192, 28672, 80, 32000
     cfg = lq.Config.make(D, H, L, 64, 8, V, 4096)
     nmat = L * (2 * D * D + 2 * D * 1024 + 3 * D * H)
-    wbytes = (nmat * 0.5 + nmat // 64 * 4) / world + V * D * (0.5 + 4 / 64)
+    peak, _ = peaks()
 
-    def measure(allreduce):
-        gid = None
-        if world > 1:
-            buf = torch.zeros(128, dtype=torch.uint8, device="cuda")
-            if rank == 0:
-                buf.copy_(torch.frombuffer(bytearray(lq.tp_unique_id()), dtype=torch.uint8))
-            dist.broadcast(buf, 0)
-            gid = bytes(buf.cpu().numpy().tobytes())
+    def measure(allreduce, size, trace=False):
+        wbytes = (nmat * 0.5 + nmat // 64 * 4) / size + V * D * (0.5 + 4 / 64)
+        grp = dist if size > 1 else None
+        gid = _group_id(lq, torch, rank if size > 1 else 0, size, grp)
         if allreduce:
             os.environ["LQ_TP_ALLREDUCE"] = allreduce
-        else:
-            os.environ.pop("LQ_TP_ALLREDUCE", None)
         t0 = time.perf_counter()
-        t = lq.Transformer.random_tp(cfg, lq.KIND_INT4, 64, 23, rank, world, gid, ctx + steps1 + 16)
+        try:
+            t = lq.Transformer.random_tp(cfg, lq.KIND_INT4, 64, 23, rank if size > 1 else 0, size, gid,
+                                         ctx + steps1 + 16)
+        finally:
+            os.environ.pop("LQ_TP_ALLREDUCE", None)
         init_s = time.perf_counter() - t0
-        os.environ.pop("LQ_TP_ALLREDUCE", None)
-        runs = []
+        runs, breakdown = [], None
         for B in (1, 16):
             steps = steps1 if B == 1 else steps16
             if B > 1:
@@ -334,36 +525,59 @@ def tp_bench(lq, torch, rank, world, dist, ctx: int = 2048, steps1: int = 16, st
             tok = np.ones(B, np.int32)
             for w in range(3):
                 tok = t.forward_batch_argmax(tok, np.full(B, ctx - 3 + w, np.int32))
-            if dist:
-                dist.barrier()
+            if grp:
+                grp.barrier()
             torch.cuda.synchronize()
             t1 = time.perf_counter()
             for s_ in range(steps):
                 tok = t.forward_batch_argmax(tok, np.full(B, ctx + s_, np.int32))
             dt = (time.perf_counter() - t1) / steps
-            if dist:
+            if grp:
                 m = torch.tensor([dt], device="cuda")
-                dist.all_reduce(m, op=dist.ReduceOp.MAX)
+                grp.all_reduce(m, op=grp.ReduceOp.MAX)
                 dt = float(m.item())
-            kv = B * 2 * L * (1024 / world) * 4 * (ctx + steps / 2)
+            kv = B * 2 * L * (1024 / size) * 4 * (ctx + steps / 2)
+            gbs = (wbytes + kv) / dt / 1e9
             runs.append({"batch": B, "tok_s": round(B / dt, 1), "ms_per_step": round(1e3 * dt, 3),
                          "weight_bytes_per_gpu": int(wbytes), "kv_bytes_per_gpu_per_step": int(kv),
-                         "hbm_gbs_per_gpu": round((wbytes + kv) / dt / 1e9, 1),
+                         "hbm_gbs_per_gpu": round(gbs, 1), "roofline_frac": round(gbs / peak, 4),
                          "path": "tcgen05 kind::i8" if B >= 16 else "dp4a GEMV"})
+            if trace and B == 1:
+                breakdown = step_breakdown(lq, t, [int(tok[0])], ctx + steps)
         t.close()
-        return runs, init_s
+        return runs, init_s, breakdown
 
-    runs, init_s = measure(None)
     out = {"config": "config5: llama-2-70b shape, int4 gs64, tensor parallel x%d, context %d" % (world, ctx),
            "split": "wq/wk/wv/w1/w3 rows, wo/w2 columns; the wo / w2 partials are summed over the processes "
                     "by the next quantizer, reading the peers' partials over NVLink (in the decode graph)",
            "timing": "max over processes of the wall clock around the timed forward_batch_argmax calls",
            "kv_note": "cache positions below the context are zero-filled, not decoded",
-           "init_s": round(init_s, 1), "runs": runs}
+           "roofline": "roofline_frac = (this GPU's weight + KV bytes per step / step time) / measured HBM peak"}
     if world > 1:
-        nccl_runs, _ = measure("nccl")
+        one = None
+        if rank == 0:
+            one, _, _ = measure(None, 1)
+        if dist:
+            dist.barrier()
+        if rank == 0:
+            out["one_gpu_runs"] = [{"batch": r["batch"], "tok_s": r["tok_s"], "ms_per_step": r["ms_per_step"]}
+                                   for r in one]
+    runs, init_s, breakdown = measure(None, world, trace=True)
+    out["init_s"] = round(init_s, 1)
+    out["runs"] = runs
+    out["step_breakdown_batch1_rank%d" % rank] = breakdown
+    if world > 1 and rank == 0:
+        out["speedup_vs_1gpu"] = {str(r["batch"]): round(r["tok_s"] / o["tok_s"], 3)
+                                  for r, o in zip(runs, out["one_gpu_runs"])}
+        out["efficiency"] = {k: round(v / world, 3) for k, v in out["speedup_vs_1gpu"].items()}
+    if world > 1:
+        nccl_runs, _, _ = measure("nccl", world)
         out["nccl_allreduce_runs"] = [{"batch": r["batch"], "tok_s": r["tok_s"], "ms_per_step": r["ms_per_step"]}
                                       for r in nccl_runs]
+    try:
+        out["tp_check"] = tp_check(lq, torch, rank, world, dist)
+    except Exception as e:
+        out["tp_check"] = {"error": str(e)[:300]}
     return out
 
 
@@ -480,11 +694,59 @@ def run_gpu(args):
     for g in graphs:
         lq.graph_destroy(g)
 
+    # per-shape device time: for each shape, a graph of back-to-back products
+    # of that shape cycling through enough copies of the matrix that they
+    # exceed 4x L2 (126 MB), so every product streams from HBM
+    per_shape = {}
+    if not args.no_per_shape:
+        ps_keep = []
+        with torch.cuda.stream(stream):
+            for i, (n, d) in enumerate(SHAPES):
+                key = f"{n}x{d}"
+                if key in per_shape:
+                    continue
+                nb = gemv_bytes(n, d, GS, KIND)
+                ncopy = max(4, -(-4 * 126 * 2**20 // nb))
+                ws_ = []
+                for c in range(ncopy):
+                    q = torch.empty((d, n), dtype=torch.uint8, device="cuda")
+                    sc = torch.empty((d, n // GS), dtype=torch.float32, device="cuda")
+                    w = lq.QuantizedTensor(q=q.data_ptr(), s=sc.data_ptr(), rows=d, cols=n, group_size=GS, kind=KIND)
+                    lq.synth_tensor(w, 2000 + rank, 10 * i + c, 0.02)
+                    ws_.append(w)
+                    ps_keep += [q, sc]
+                reps = max(ncopy, 16)
+                lq.set_launch_flags(lq.LAUNCH_PDL)
+                lq.graph_begin()
+                for r_ in range(reps):
+                    lq.matmul_f32(ys[i].data_ptr(), xs[i].data_ptr(), ws_[r_ % ncopy], n, d)
+                g = lq.graph_end()
+                lq.set_launch_flags(0)
+                for _ in range(3):
+                    lq.graph_launch(g)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                for _ in range(5):
+                    lq.graph_launch(g)
+                e1.record(stream)
+                e1.synchronize()
+                us = e0.elapsed_time(e1) * 1e3 / (5 * reps)
+                lq.graph_destroy(g)
+                per_shape[key] = {"us": round(us, 3), "bytes": nb, "gbs": round(nb / us / 1e3, 1),
+                                  "copies": ncopy}
+        del ps_keep
+        stream.synchronize()
+
     extra = {}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         gbs, kind, cores, desc, _ = cpu_baseline(seconds=args.cpu_seconds)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc}
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind, "sample": desc,
+               "cpu": cpu_model()}
+        try:
+            extra["reference_decode_cpu"] = cpu_decode_baselines(with_7b=False)
+        except Exception as e:
+            extra["reference_decode_cpu"] = {"error": str(e)[:300]}
     if rank == 0 and world == 1 and not args.no_decode:
         try:
             extra["decode"] = decode_bench(lq, torch, args.decode_positions)
@@ -504,6 +766,8 @@ def run_gpu(args):
 
     if rank == 0:
         peak, peak_kind = peaks()
+        for v in per_shape.values():
+            v["frac"] = round(v["gbs"] / peak, 4)
         tr = traffic_per_launch()
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -513,17 +777,22 @@ def run_gpu(args):
             "config": {"workload": WORKLOAD, "group_size": GS, "weight_kind": "int8", "batch": 1,
                        "bytes_per_step": sb, "l2": f"{COPIES} weight copies ({COPIES * sb / 1e9:.2f} GB) alternate; "
                        "inputs larger than L2", "parallelism": f"replicas x{world}",
-                       "launch": "CUDA graph per step: 8 x (activation quantizer + GEMV), programmatic dependent launch"},
+                       "launch": "CUDA graph per step: 8 GEMV launches (each quantizes its fp32 input in its "
+                                 "prologue), programmatic dependent launch",
+                       "per_shape_us": per_shape},
             "roofline": {"bound": "hbm", "achieved": round(per_gpu_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(per_gpu_gbs / peak, 4), "peak_source": peak_kind,
                          "kernel": "lq::gemv_tma_kernel<8,1>",
-                         "traffic": (tr or {}).get("dram_bytes_per_step_scaled")},
+                         "traffic": (tr or {}).get("dram_bytes_per_step_scaled"),
+                         "traffic_source": ("copied from profiles/gemv_traffic.json (ncu dram__bytes_read.sum + "
+                                            "dram__bytes_write.sum of the sweep's launches), not measured in this run")
+                         if tr else None},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "steps": e2e_steps,
                     "h2d_bytes_per_step": sum(4 * n for n, d in SHAPES),
                     "d2h_bytes_per_step": sum(4 * d for n, d in SHAPES),
                     "path": "matmul_f32 C ABI, pinned host x and y, copies + sync inside each call"},
-            "gpu_launches": args.steps * 2 * len(SHAPES),
+            "gpu_launches": args.steps * len(SHAPES),
             "clocks": clk,
         }
         line.update(extra)
@@ -545,6 +814,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-batch", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
+    ap.add_argument("--no-per-shape", action="store_true")
     ap.add_argument("--probe", default=None, help="LAYERS:BATCH:KIND:CTX: one small 13B-shape step for profilers")
     args = ap.parse_args()
     if args.warmup < 3:

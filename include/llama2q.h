@@ -183,6 +183,21 @@ float* forward(Transformer* t, int token, int pos);
  * to *next_token and copies 4 bytes instead of the logits. */
 int forward_argmax(Transformer* t, int token, int pos, int* next_token);
 
+/* Prompt prefill for sequence 0: tokens[0 .. n_tokens) at positions
+ * start_pos .. start_pos + n_tokens - 1, written into the KV cache as if fed
+ * one at a time.  The prompt runs in steps of up to 64 tokens whose rows go
+ * through every product together (from 16 rows on, the tensor-core GEMM: the
+ * weights are read once per step, not once per token), each row attending
+ * causally over the cache up to its own position.  Returns host logits
+ * [vocab] of the last prompt token (owned by t, valid until the next call),
+ * or NULL on error.  Replaces the whole-sequence prompt forward of
+ * v2-cuda/run.cu:347-394 (matmul_q8_kernel over T rows, :131-162, causal
+ * attention :194-238) and the one-token-at-a-time prompt loop of runq.c's
+ * generate (v1-int8-vnni/runq.c:691-703).  Rows below 16 use the GEMV, whose
+ * per-row arithmetic is that of forward(); from 16 rows the per-row fp32
+ * order is the tensor-core GEMM's. */
+float* forward_prompt(Transformer* t, const int* tokens, int n_tokens, int start_pos);
+
 /* ---- batched decode (B independent sequences, one token each per step) ---
  * The reference decodes one sequence; its batched kernel is the prompt-time
  * matmul_q8_kernel of v2-cuda/run.cu:131-162 (T rows against one weight
@@ -251,6 +266,28 @@ int lq_tp_wait_selftest(int tp_size, int wait_us, double* first_ms, double* seco
 /* Release a model (free_transformer, runq.c:285-289). */
 void free_transformer(Transformer* t);
 
+/* ---- step trace (profiling; no counterpart in the reference) -------------
+ * With tracing on, every kernel of a decode step records three device-clock
+ * stamps (globaltimer, ns): when its first CTA started, when its first CTA
+ * got past the wait for the previous kernel (programmatic dependent launch),
+ * and when its last warp finished.  Read them after a step to see where the
+ * step's time goes (the reference times whole tokens only,
+ * v1-int8-vnni/runq.c:710-716).  Turning tracing on or off re-captures the
+ * step's graph at the next step. */
+#define LQ_TRACE_QUANT 1      /* activation quantizer */
+#define LQ_TRACE_GEMV 2       /* batch-1..8 GEMV */
+#define LQ_TRACE_QGEMM 3      /* tensor-core GEMM */
+#define LQ_TRACE_ATTENTION 4  /* split-KV attention */
+#define LQ_TRACE_ALLREDUCE 5  /* tensor-parallel all-reduce fused into the quantizer */
+#define LQ_TRACE_ARGMAX 6
+#define LQ_TRACE_NCCL 7       /* NCCL all-reduce: a library kernel, no stamps (all bits set) */
+int transformer_trace(Transformer* t, int enable);
+/* After a step: *count = kernels in the step; for the first min(count,
+ * max_kernels) kernels in launch order, kinds[i] (LQ_TRACE_*) and stamps[3i ..
+ * 3i+2] = start, past-wait, end.  A stamp with all bits set was not recorded
+ * (a kernel whose CTAs all exited before that point, or an NCCL kernel). */
+int transformer_trace_read(Transformer* t, int max_kernels, int* kinds, uint64_t* stamps, int* count);
+
 /* Copy out the model's shape, weight kind and group size. */
 int transformer_config(const Transformer* t, Config* cfg, int* kind, int* group_size);
 
@@ -268,6 +305,14 @@ int lq_write_checkpoint_fp32(const char* path, const Config* cfg, uint64_t seed,
  * tools/quantize_int4.py:54-115).  group_size 32 writes the reference's own
  * version 1 / 2 files; any other group size writes version 3. */
 int lq_quantize_checkpoint(const char* src_fp32, const char* dst, int kind, int group_size);
+
+/* Write a quantized checkpoint of seeded synthetic weights directly: the
+ * bytes lq_write_checkpoint_fp32 (unshared classifier) followed by
+ * lq_quantize_checkpoint would give, without the fp32 file (a 7B fp32
+ * export is 27 GB).  Group size 32 writes the reference's version 1 (INT8) /
+ * 2 (INT4) files; others version 3.  Uses all host threads (OpenMP). */
+int lq_write_checkpoint_random(const char* path, const Config* cfg, int kind, int group_size, uint64_t seed,
+                               float std);
 
 /* Read only the header of a quantized checkpoint. */
 int lq_read_header(const char* path, Config* cfg, int* kind, int* group_size, int* shared);

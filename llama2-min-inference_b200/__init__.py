@@ -31,6 +31,9 @@ KIND_ACT8 = 1
 
 OK, EINVAL, ECUDA, ENOMEM, EIO, EFORMAT, ETIMEOUT, EUNSUPPORTED = range(8)
 
+# step-trace kernel kinds (transformer_trace_read)
+TRACE_KINDS = {1: "quantize", 2: "gemv", 3: "qgemm", 4: "attention", 5: "allreduce", 6: "argmax", 7: "nccl"}
+
 # tensor ids of the checkpoint (file order) = synthetic generator streams
 T_EMB, T_RMS_ATT, T_WQ, T_WK, T_WV, T_WO, T_RMS_FFN, T_W1, T_W2, T_W3, T_RMS_FINAL, T_WCLS = range(12)
 
@@ -81,11 +84,12 @@ EXPORTS = (
     "lq_last_error", "lq_select_device", "lq_set_stream", "lq_get_stream", "lq_sync",
     "lq_set_launch_flags", "lq_set_trace", "lq_graph_begin", "lq_graph_end", "lq_graph_launch", "lq_graph_destroy",
     "lq_synth_tensor", "quantize", "matmul", "matmul_f32", "matmul_f32_noalloc",
-    "build_transformer", "build_transformer_random", "forward", "forward_argmax",
+    "build_transformer", "build_transformer_random", "forward", "forward_argmax", "forward_prompt",
     "transformer_reserve_batch", "forward_batch", "forward_batch_argmax",
     "lq_tp_unique_id", "build_transformer_tp", "build_transformer_random_tp", "lq_tp_wait_selftest",
-    "free_transformer", "transformer_config",
-    "lq_write_checkpoint_fp32", "lq_quantize_checkpoint", "lq_read_header", "lq_synth_value",
+    "free_transformer", "transformer_config", "transformer_trace", "transformer_trace_read",
+    "lq_write_checkpoint_fp32", "lq_quantize_checkpoint", "lq_write_checkpoint_random", "lq_read_header",
+    "lq_synth_value",
 )
 
 _lib = None
@@ -123,6 +127,7 @@ def lib() -> C.CDLL:
         "build_transformer_random": (I, [C.POINTER(P), CFG, I, I, U64, I]),
         "forward": (C.POINTER(F), [P, I, I]),
         "forward_argmax": (I, [P, I, I, C.POINTER(I)]),
+        "forward_prompt": (C.POINTER(F), [P, P, I, I]),
         "transformer_reserve_batch": (I, [P, I]),
         "lq_tp_unique_id": (I, [P]),
         "lq_tp_wait_selftest": (I, [I, I, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
@@ -132,8 +137,11 @@ def lib() -> C.CDLL:
         "forward_batch_argmax": (I, [P, P, P, I, P]),
         "free_transformer": (None, [P]),
         "transformer_config": (I, [P, CFG, C.POINTER(I), C.POINTER(I)]),
+        "transformer_trace": (I, [P, I]),
+        "transformer_trace_read": (I, [P, I, P, P, C.POINTER(I)]),
         "lq_write_checkpoint_fp32": (I, [C.c_char_p, CFG, U64, F, I]),
         "lq_quantize_checkpoint": (I, [C.c_char_p, C.c_char_p, I, I]),
+        "lq_write_checkpoint_random": (I, [C.c_char_p, CFG, I, I, U64, F]),
         "lq_read_header": (I, [C.c_char_p, CFG, C.POINTER(I), C.POINTER(I), C.POINTER(I)]),
         "lq_synth_value": (F, [U64, I, U64, F]),
     }
@@ -249,6 +257,17 @@ class Transformer:
             raise LlamaQError(-1, last_error())
         return np.ctypeslib.as_array(p, shape=(self.config.vocab_size,))
 
+    def forward_prompt(self, tokens, start_pos: int = 0):
+        """Prefill sequence 0 with the prompt tokens at start_pos..; returns a
+        numpy view of the last token's logits (valid until the next call)."""
+        import numpy as np
+
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        p = lib().forward_prompt(self._h, t.ctypes.data, t.size, start_pos)
+        if not p:
+            raise LlamaQError(-1, last_error())
+        return np.ctypeslib.as_array(p, shape=(self.config.vocab_size,))
+
     def forward_argmax(self, token: int, pos: int) -> int:
         nxt = C.c_int()
         check(lib().forward_argmax(self._h, token, pos, C.byref(nxt)))
@@ -304,6 +323,21 @@ class Transformer:
         check(lib().forward_batch_argmax(self._h, t.ctypes.data, p.ctypes.data, t.size, out.ctypes.data))
         return out
 
+    def trace(self, enable: bool = True) -> None:
+        """Turn the step trace on or off (the graph is captured again)."""
+        check(lib().transformer_trace(self._h, 1 if enable else 0))
+
+    def trace_read(self):
+        """(kinds [K], stamps [K, 3] uint64 ns: start, past-wait, end) of the last step."""
+        import numpy as np
+
+        cnt = C.c_int()
+        check(lib().transformer_trace_read(self._h, 0, None, None, C.byref(cnt)))
+        k = np.zeros(cnt.value, np.int32)
+        st = np.zeros((cnt.value, 3), np.uint64)
+        check(lib().transformer_trace_read(self._h, cnt.value, k.ctypes.data, st.ctypes.data, C.byref(cnt)))
+        return k, st
+
     def close(self) -> None:
         if self._h:
             lib().free_transformer(self._h)
@@ -345,6 +379,12 @@ def write_checkpoint_fp32(path: str, cfg: Config, seed: int, std: float = 0.02, 
 
 def quantize_checkpoint(src: str, dst: str, kind: int, group_size: int) -> None:
     check(lib().lq_quantize_checkpoint(src.encode(), dst.encode(), kind, group_size))
+
+
+def write_checkpoint_random(path: str, cfg: Config, kind: int, group_size: int, seed: int, std: float = 0.02) -> None:
+    """Seeded quantized checkpoint written directly (same bytes as the fp32
+    export + quantize_checkpoint, unshared classifier)."""
+    check(lib().lq_write_checkpoint_random(path.encode(), C.byref(cfg), kind, group_size, seed, std))
 
 
 def read_header(path: str):

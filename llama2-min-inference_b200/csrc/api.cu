@@ -93,6 +93,8 @@ int check_device_error(int* err_dev, cudaStream_t st) {
 }
 
 cudaStream_t stream() { return g_stream; }
+int launch_flags() { return g_launch_flags; }
+uint64_t* trace_buffer() { return g_trace; }
 
 // quantize x into (xq, xs, xsum), then the GEMV from the pre-quantized
 // activation; the GEMV may start streaming weights while the quantizer runs
@@ -383,14 +385,25 @@ int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int
     DevCtx* c = ctx();
     if (!c) return lq_fail(LQ_ECUDA, "no CUDA device context (no device, or first use inside a graph capture)");
     const bool xdev = is_device_ptr(x), ydev = is_device_ptr(xout);
+    if ((reinterpret_cast<uintptr_t>(x) & 15u) && xdev)
+        return lq_fail(LQ_EINVAL, "matmul_f32: device x must be 16-byte aligned");
+    static int fused = -1;
+    if (fused < 0) {
+        const char* e = getenv("LQ_MATMUL_FUSED");
+        fused = e ? atoi(e) : 0;
+    }
     const int ng = n / w->group_size;
-    // scratch: [fp32 x (host input only)] [int8 xq] [fp32 xs] [int32 xsum] [fp32 y (host output only)]
-    const size_t off_xq = xdev ? 0 : ((size_t)n * 4 + 255) / 256 * 256;
-    const size_t off_xs = off_xq + ((size_t)n + 255) / 256 * 256;
-    const size_t off_xsum = off_xs + ((size_t)ng * 4 + 255) / 256 * 256;
-    const size_t off_y = off_xsum + ((size_t)ng * 4 + 255) / 256 * 256;
-    rc = ensure_scratch(c, off_y + (ydev ? 0 : (size_t)d * 4));
-    if (rc) return rc;
+    auto up = [](size_t v) { return (v + 255) / 256 * 256; };
+    // scratch: [fp32 x (host input)] [fp32 y (host output)] and, for the
+    // two-launch form, [int8 xq] [fp32 xs] [int32 xsum]
+    const size_t off_y = xdev ? 0 : up((size_t)n * 4);
+    const size_t off_xq = off_y + (ydev ? 0 : up((size_t)d * 4));
+    const size_t off_xs = off_xq + up((size_t)n), off_xsum = off_xs + up((size_t)ng * 4);
+    const size_t need = fused ? off_xq : off_xsum + up((size_t)ng * 4);
+    if (need) {
+        rc = ensure_scratch(c, need);
+        if (rc) return rc;
+    }
     char* sc = static_cast<char*>(c->scratch);
     const float* xd = x;
     float* yd = ydev ? xout : reinterpret_cast<float*>(sc + off_y);
@@ -399,10 +412,29 @@ int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int
         if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of x");
         xd = reinterpret_cast<const float*>(sc);
     }
-    rc = lq::matmul_f32_device(yd, xd, w, n, d, reinterpret_cast<int8_t*>(sc + off_xq),
-                               reinterpret_cast<float*>(sc + off_xs), reinterpret_cast<int*>(sc + off_xsum),
-                               c->err, g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms, g_trace);
-    if (rc) return rc;
+    if (fused) {
+        // one launch: every CTA quantizes x in its prologue (quantize_act's
+        // arithmetic, runq.c:117-139) while its first weight copies are in flight
+        GemvArgs a = {};
+        a.seg[0] = {static_cast<const uint8_t*>(w->q), w->s, yd, d, EPI_STORE};
+        a.nseg = 1;
+        a.cols = n;
+        a.gs = w->group_size;
+        a.nb = 1;
+        a.in_mode = IN_F32;
+        a.xf = xd;
+        a.y_stride = d;
+        a.err = c->err;
+        a.trace = g_trace;
+        cudaError_t e = gemv_launch(a, w->kind, g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms);
+        if (e != cudaSuccess) return cuda_fail(e, "matmul_f32 launch");
+    } else {
+        // the activation quantizer, then the GEMV from the int8 activation
+        rc = lq::matmul_f32_device(yd, xd, w, n, d, reinterpret_cast<int8_t*>(sc + off_xq),
+                                   reinterpret_cast<float*>(sc + off_xs), reinterpret_cast<int*>(sc + off_xsum), c->err,
+                                   g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms, g_trace);
+        if (rc) return rc;
+    }
     if (!xdev || !ydev) {
         cudaError_t e = cudaSuccess;
         if (!ydev) e = cudaMemcpyAsync(xout, yd, (size_t)d * 4, cudaMemcpyDeviceToHost, g_stream);

@@ -225,6 +225,86 @@ int lq_quantize_checkpoint(const char* src, const char* dst, int kind, int gs) {
     return LQ_OK;
 }
 
+/* ---- seeded quantized writer ---------------------------------------------
+ * The same bytes lq_write_checkpoint_fp32 followed by lq_quantize_checkpoint
+ * would produce (same generator, same quantizer), written block by block
+ * without the fp32 intermediate; rows are generated and quantized in
+ * parallel (OpenMP). */
+
+static int put_synth_q(FILE* f, uint64_t seed, int tid, int64_t rows, int64_t cols, int gs, int kind, float std) {
+    const int64_t rb = kind == LQ_KIND_INT8 ? cols : cols / 2, ng = cols / gs;
+    const int64_t blk = 256;
+    float* w = (float*)malloc((size_t)(blk * cols) * 4);
+    uint8_t* q = (uint8_t*)malloc((size_t)(blk * rb));
+    float* s = (float*)malloc((size_t)(rows * ng) * 4);
+    if (!w || !q || !s) {
+        free(w);
+        free(q);
+        free(s);
+        return LQ_ENOMEM;
+    }
+    int rc = LQ_OK;
+    for (int64_t r0 = 0; r0 < rows && rc == LQ_OK; r0 += blk) {
+        const int64_t m = rows - r0 < blk ? rows - r0 : blk;
+#pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < m; r++) {
+            for (int64_t c = 0; c < cols; c++)
+                w[r * cols + c] = lq_synth_value(seed, tid, (uint64_t)((r0 + r) * cols + c), std);
+            lq_quantize_rows_host(w + r * cols, 1, cols, gs, kind, q + r * rb, s + (r0 + r) * ng);
+        }
+        if (fwrite(q, 1, (size_t)(m * rb), f) != (size_t)(m * rb)) rc = LQ_EIO;
+    }
+    if (rc == LQ_OK && fwrite(s, 4, (size_t)(rows * ng), f) != (size_t)(rows * ng)) rc = LQ_EIO;
+    free(w);
+    free(q);
+    free(s);
+    return rc;
+}
+
+static int put_synth_f32(FILE* f, uint64_t seed, int tid, int64_t n, float std, int ones) {
+    const int64_t blk = (int64_t)1 << 20;
+    float* buf = (float*)malloc((size_t)blk * 4);
+    if (!buf) return LQ_ENOMEM;
+    int rc = LQ_OK;
+    for (int64_t i = 0; i < n && rc == LQ_OK; i += blk) {
+        const int64_t m = n - i < blk ? n - i : blk;
+#pragma omp parallel for schedule(static)
+        for (int64_t j = 0; j < m; j++) buf[j] = ones ? 1.0f : lq_synth_value(seed, tid, (uint64_t)(i + j), std);
+        if (fwrite(buf, 4, (size_t)m, f) != (size_t)m) rc = LQ_EIO;
+    }
+    free(buf);
+    return rc;
+}
+
+int lq_write_checkpoint_random(const char* path, const Config* cfg, int kind, int gs, uint64_t seed, float std) {
+    LqTensorDesc t[LQ_NT];
+    if (!path || !cfg || lq_tensor_table(cfg, t) != LQ_OK)
+        return lq_fail(LQ_EINVAL, "lq_write_checkpoint_random: bad config");
+    if (kind != LQ_KIND_INT8 && kind != LQ_KIND_INT4)
+        return lq_fail(LQ_EINVAL, "lq_write_checkpoint_random: kind must be INT8 or INT4");
+    if (gs <= 0 || gs % 32 != 0 || gs > 256 || cfg->dim % gs || cfg->hidden_dim % gs)
+        return lq_fail(LQ_EINVAL, "lq_write_checkpoint_random: group size %d", gs);
+    FILE* f = fopen(path, "wb");
+    if (!f) return lq_fail(LQ_EIO, "cannot open %s for writing", path);
+    const uint32_t magic = kind == LQ_KIND_INT8 ? LQ_MAGIC_Q8 : LQ_MAGIC_Q4;
+    const uint32_t version = gs == 32 ? (kind == LQ_KIND_INT8 ? 1u : 2u) : 3u;
+    const int32_t hdr[7] = {cfg->dim, cfg->hidden_dim, cfg->n_layers, cfg->n_heads,
+                            cfg->n_kv_heads, -cfg->vocab_size, cfg->seq_len};
+    const int32_t g = gs;
+    int rc = (fwrite(&magic, 4, 1, f) == 1 && fwrite(&version, 4, 1, f) == 1 && fwrite(hdr, 4, 7, f) == 7 &&
+              (version != 3 || fwrite(&g, 4, 1, f) == 1))
+                 ? LQ_OK
+                 : LQ_EIO;
+    for (int i = 0; i < LQ_NT && rc == LQ_OK; i++) {
+        const int ones = t[i].id == LQ_T_RMS_ATT || t[i].id == LQ_T_RMS_FFN || t[i].id == LQ_T_RMS_FINAL;
+        rc = t[i].quantized ? put_synth_q(f, seed, t[i].id, t[i].rows, t[i].cols, gs, kind, std)
+                            : put_synth_f32(f, seed, t[i].id, t[i].rows * t[i].cols, std, ones);
+    }
+    if (fclose(f) != 0 && rc == LQ_OK) rc = LQ_EIO;
+    if (rc != LQ_OK) return lq_fail(rc, "write failed: %s", path);
+    return LQ_OK;
+}
+
 /* ---- reader ------------------------------------------------------------- */
 
 int lq_parse_header(const uint8_t* p, size_t size, Config* cfg, int* kind, int* gs, int* shared,

@@ -50,6 +50,13 @@ constexpr int kCT = kW * 32;
 
 __host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
+// The stand-alone activation quantizer's thread count.  The rmsnorm sum of
+// squares is defined by its reduction order (256 threads, thread t takes
+// float4 chunks t, t+256, ...; warps summed in order), which the GEMV
+// prologue reproduces whatever its own thread count.
+constexpr int kAqThreads = 256;
+constexpr int kRedFloats = kAqThreads + 8;  // shared reduction scratch of the prologue
+
 struct Layout {
     int off_bars, off_red, off_x, off_xs, off_xsum, off_stage, stage_bytes, total;
 };
@@ -59,7 +66,7 @@ __host__ __device__ inline Layout make_layout(const GemvArgs& a) {
     const int ng = a.cols / a.gs;
     L.off_bars = 0;
     L.off_red = align_up(a.nstages * 8, 16);
-    L.off_x = align_up(L.off_red + 32 * 4, 128);
+    L.off_x = align_up(L.off_red + kRedFloats * 4, 128);
     L.off_xs = align_up(L.off_x + a.x_bytes, 16);
     L.off_xsum = align_up(L.off_xs + a.nb * ng * 4, 16);
     L.off_stage = align_up(L.off_xsum + a.nb * ng * 4, 128);
@@ -91,37 +98,77 @@ __device__ __forceinline__ int quant_div(float x, float s, float rcp) {
     return (int)r;
 }
 
-// Deterministic sum over the consumer threads (same order in every CTA).
-__device__ float consumer_sum(float v, float* red, int ctid, int nt) {
-    v = warp_sum(v);
-    if ((ctid & 31) == 0) red[ctid >> 5] = v;
+// rmsnorm scale 1/sqrt(mean(x^2) + 1e-5) (v1-int8-vnni/runq.c:294-305) with
+// the sum of squares associated exactly as act_quant_kernel associates it:
+// virtual thread t (0..255) takes float4 chunks t, t+256, ... with fmaf,
+// each virtual warp is summed by the xor butterfly, the eight warp sums are
+// added in order.  nt real threads (any multiple of 32) stand in for the 256.
+__device__ float rms_inv_aq(const float* src, int n, float* red, int ctid, int nt) {
+    const int nc = n >> 2;
+    for (int vt = ctid; vt < kAqThreads; vt += nt) {
+        float ss = 0.0f;
+        int c = vt;
+        for (; c + 3 * kAqThreads < nc; c += 4 * kAqThreads) {
+            float4 q[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) q[u] = reinterpret_cast<const float4*>(src)[c + u * kAqThreads];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                ss = fmaf(q[u].x, q[u].x, ss);
+                ss = fmaf(q[u].y, q[u].y, ss);
+                ss = fmaf(q[u].z, q[u].z, ss);
+                ss = fmaf(q[u].w, q[u].w, ss);
+            }
+        }
+        for (; c < nc; c += kAqThreads) {
+            const float4 q = reinterpret_cast<const float4*>(src)[c];
+            ss = fmaf(q.x, q.x, ss);
+            ss = fmaf(q.y, q.y, ss);
+            ss = fmaf(q.z, q.z, ss);
+            ss = fmaf(q.w, q.w, ss);
+        }
+        red[vt] = ss;
+    }
     named_bar_sync(1, nt);
-    float s = 0.0f;
-    for (int w = 0; w < nt / 32; ++w) s += red[w];
+    if (ctid < 32) {
+        float t = 0.0f;
+        for (int w = 0; w < kAqThreads / 32; ++w) t += warp_sum(red[w * 32 + ctid]);
+        if (ctid == 0) red[kAqThreads] = t;
+    }
     named_bar_sync(1, nt);
-    return s;
+    const float t = red[kAqThreads];
+    named_bar_sync(1, nt);  // red is reused by the next activation row
+    return 1.0f / sqrtf(t / (float)n + 1e-5f);
 }
 
+// Build the int8 activation of the launch's rows in shared memory: group
+// sums and scales for groups [g0, g1) of every row (all groups when the CTA
+// is not part of a cluster; a cluster's CTAs then exchange their slices).
 template <int KIND>
-__device__ void stage_input(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum, float* red, int ctid, int nt) {
+__device__ void stage_input(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum, float* red, int ctid, int nt,
+                            int g0, int g1) {
     const int n = a.cols, gs = a.gs, ng = n / gs;
     if (a.in_mode == IN_QUANT) {
         // copy int8 rows (INT4: split into even/odd planes), 8 bytes a step;
         // every load of this thread is issued before any store
-        const int total8 = a.nb * n / 8;
+        const int upr = (g1 - g0) * gs / 8;  // 8-byte units of one row's slice
+        const int total8 = a.nb * upr;
         constexpr int U = 4;
         for (int i0 = ctid; i0 < total8; i0 += U * nt) {
             uint2 v[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int i = i0 + u * nt;
-                if (i < total8) v[u] = reinterpret_cast<const uint2*>(a.xq)[i];
+                if (i < total8) {
+                    const int b = i / upr, k0 = g0 * gs + (i - b * upr) * 8;
+                    v[u] = *reinterpret_cast<const uint2*>(a.xq + (size_t)b * n + k0);
+                }
             }
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const int i = i0 + u * nt;
                 if (i >= total8) break;
-                const int b = (i * 8) / n, k0 = i * 8 - b * n;
+                const int b = i / upr, k0 = g0 * gs + (i - b * upr) * 8;
                 int8_t* xrow = xsm + (size_t)b * n;
                 if (KIND == 4) {
                     *reinterpret_cast<uint32_t*>(xrow + (k0 >> 1)) = __byte_perm(v[u].x, v[u].y, 0x6420);
@@ -131,8 +178,10 @@ __device__ void stage_input(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum
                 }
             }
         }
+        const int sg = g1 - g0;
         if (a.xsum_in) {
-            for (int g = ctid; g < a.nb * ng; g += nt) {
+            for (int i = ctid; i < a.nb * sg; i += nt) {
+                const int g = (i / sg) * ng + g0 + i % sg;
                 xs[g] = a.xs[g];
                 xsum[g] = a.xsum_in[g];
             }
@@ -140,8 +189,8 @@ __device__ void stage_input(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum
             named_bar_sync(1, nt);
             // group sums from the staged copy (INT4: the group's even and odd
             // values are two contiguous runs of gs/2 bytes, one per plane)
-            for (int g = ctid; g < a.nb * ng; g += nt) {
-                const int b = g / ng, gg = g - b * ng;
+            for (int i = ctid; i < a.nb * sg; i += nt) {
+                const int b = i / sg, gg = g0 + i % sg, g = b * ng + gg;
                 const int8_t* xrow = xsm + (size_t)b * n;
                 int s = 0;
                 if (KIND == 4) {
@@ -158,11 +207,26 @@ __device__ void stage_input(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum
         }
         return;
     }
-    constexpr int MAXR = 8;  // rounds of 8 values per thread held in registers
+    // quantize_act (runq.c:117-139), optionally after rmsnorm: thread t of a
+    // pass takes 8 consecutive values; a group spans gs/8 consecutive lanes,
+    // whose max and sum come from xor shuffles.  The loop is kept rolled (one
+    // copy of its body): these kernels are short, and every instruction of
+    // the prologue is fetched cold.
     const bool norm = a.in_mode == IN_RMSNORM || a.in_mode == IN_RMSNORM_EMB;
     const int lpg = gs / 8;   // lanes per group: 4, 8, 16 or 32
-    const int tasks = ng * lpg;
+    const int nvalid = (a.nvalid > 0 && a.nvalid < a.nb) ? a.nvalid : a.nb;
     for (int b = 0; b < a.nb; ++b) {
+        int8_t* xrow = xsm + (size_t)b * n;
+        if (b >= nvalid) {
+            // padding row of a partial chunk: its inputs (and its token) lie
+            // past the caller's rows, and its results are not stored
+            for (int i = ctid * 16; i < n; i += nt * 16) *reinterpret_cast<uint4*>(xrow + i) = make_uint4(0, 0, 0, 0);
+            for (int g = ctid; g < ng; g += nt) {
+                xs[b * ng + g] = 0.0f;
+                xsum[b * ng + g] = 0;
+            }
+            continue;
+        }
         const float* src = a.xf ? a.xf + (size_t)b * n : nullptr;
         if (a.in_mode == IN_RMSNORM_EMB) {
             const int token = a.meta[2 * b];
@@ -170,87 +234,96 @@ __device__ void stage_input(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum
             if (blockIdx.x == 0)
                 for (int i = ctid; i < n; i += nt) a.x_out[(size_t)b * n + i] = src[i];
         }
-        int8_t* xrow = xsm + (size_t)b * n;
-        for (int base = 0; base < tasks; base += MAXR * nt) {
-            // all of this thread's loads first (8 values per round), then the math
-            float v[MAXR][8];
+        const float inv = norm ? rms_inv_aq(src, n, red, ctid, nt) : 1.0f;
+        // software pipelined: the next pass's loads are issued before this
+        // pass's arithmetic (tasks of groups [g0, g1) only)
+        float4 c0 = make_float4(0.f, 0.f, 0.f, 0.f), c1 = c0;
+        const int t_end = g1 * lpg;
+        if (g0 * lpg + ctid < t_end) {
+            c0 = *reinterpret_cast<const float4*>(src + (g0 * lpg + ctid) * 8);
+            c1 = *reinterpret_cast<const float4*>(src + (g0 * lpg + ctid) * 8 + 4);
+        }
+#pragma unroll 1
+        for (int base = g0 * lpg; base < t_end; base += nt) {
+            const int t = base + ctid;
+            const bool on = t < t_end;
+            float v[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            const int tn = t + nt;
+            if (tn < t_end) {
+                c0 = *reinterpret_cast<const float4*>(src + tn * 8);
+                c1 = *reinterpret_cast<const float4*>(src + tn * 8 + 4);
+            }
+            const int k0 = (on ? t : 0) * 8;
+            if (norm && on) {
+                // rmsnorm scaling w * (inv * x), as act_quant_kernel applies it
+                const float4 w0 = *reinterpret_cast<const float4*>(a.rms_w + k0);
+                const float4 w1 = *reinterpret_cast<const float4*>(a.rms_w + k0 + 4);
+                const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-            for (int r = 0; r < MAXR; ++r) {
-                const int t = base + r * nt + ctid;
-                if (t < tasks) {
-                    const float4 a0 = *reinterpret_cast<const float4*>(src + t * 8);
-                    const float4 a1 = *reinterpret_cast<const float4*>(src + t * 8 + 4);
-                    v[r][0] = a0.x; v[r][1] = a0.y; v[r][2] = a0.z; v[r][3] = a0.w;
-                    v[r][4] = a1.x; v[r][5] = a1.y; v[r][6] = a1.z; v[r][7] = a1.w;
+                for (int i = 0; i < 8; ++i) v[i] = w[i] * (inv * v[i]);
+            }
+            float amax = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            for (int o = 1; o < lpg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            float sc = amax / 127.0f;
+            if (sc == 0.0f) sc = 1e-8f;
+            const float rcp = 1.0f / sc;
+            int qs = 0;
+            if (on) {
+                int q[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    q[i] = max(-127, min(127, quant_div(v[i], sc, rcp)));
+                    qs += q[i];
+                }
+                uint32_t lo, hi;
+                if (KIND == 4) {  // even values to plane 0, odd values to plane 1
+                    lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) | ((uint32_t)(q[6] & 0xFF) << 24);
+                    hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+                    *reinterpret_cast<uint32_t*>(xrow + (k0 >> 1)) = lo;
+                    *reinterpret_cast<uint32_t*>(xrow + (n >> 1) + (k0 >> 1)) = hi;
                 } else {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) v[r][i] = 0.0f;
+                    lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
+                    hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
+                    *reinterpret_cast<uint2*>(xrow + k0) = make_uint2(lo, hi);
                 }
             }
-            if (norm) {
-                // rmsnorm, v1-int8-vnni/runq.c:294-305: 1/sqrt(mean(x^2) + 1e-5).
-                // Requires the whole vector in one pass (n <= MAXR*8*256).
-                float ss = 0.0f;
-#pragma unroll
-                for (int r = 0; r < MAXR; ++r)
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) ss = fmaf(v[r][i], v[r][i], ss);
-                ss = consumer_sum(ss, red, ctid, nt);
-                const float inv = 1.0f / sqrtf(ss / (float)n + 1e-5f);
-#pragma unroll
-                for (int r = 0; r < MAXR; ++r) {
-                    const int t = base + r * nt + ctid;
-                    if (t < tasks) {
-                        const float4 w0 = *reinterpret_cast<const float4*>(a.rms_w + t * 8);
-                        const float4 w1 = *reinterpret_cast<const float4*>(a.rms_w + t * 8 + 4);
-                        const float w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) v[r][i] = w[i] * (inv * v[r][i]);
-                    }
-                }
+            for (int o = 1; o < lpg; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+            if (on && (t & (lpg - 1)) == 0) {
+                const int g = t / lpg;
+                xs[b * ng + g] = sc;
+                xsum[b * ng + g] = qs;
             }
-            // quantize_act, runq.c:117-139: a group spans lpg lanes (8 values
-            // each); group max and sum by xor shuffles over those lanes
-#pragma unroll
-            for (int r = 0; r < MAXR; ++r) {
-                const int t = base + r * nt + ctid;
-                if (base + r * nt >= tasks) break;  // uniform across the block
-                const bool on = t < tasks;
-                const int k0 = (on ? t : 0) * 8;
-                float amax = 0.0f;
-#pragma unroll
-                for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[r][i]));
-                for (int o = 1; o < lpg; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-                float sc = amax / 127.0f;
-                if (sc == 0.0f) sc = 1e-8f;
-                const float rcp = 1.0f / sc;
-                int qs = 0;
-                if (on) {
-                    int q[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        q[i] = max(-127, min(127, quant_div(v[r][i], sc, rcp)));
-                        qs += q[i];
-                    }
-                    uint32_t lo, hi;
-                    if (KIND == 4) {  // even values to plane 0, odd values to plane 1
-                        lo = (q[0] & 0xFF) | ((q[2] & 0xFF) << 8) | ((q[4] & 0xFF) << 16) | ((uint32_t)(q[6] & 0xFF) << 24);
-                        hi = (q[1] & 0xFF) | ((q[3] & 0xFF) << 8) | ((q[5] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
-                        *reinterpret_cast<uint32_t*>(xrow + (k0 >> 1)) = lo;
-                        *reinterpret_cast<uint32_t*>(xrow + (n >> 1) + (k0 >> 1)) = hi;
-                    } else {
-                        lo = (q[0] & 0xFF) | ((q[1] & 0xFF) << 8) | ((q[2] & 0xFF) << 16) | ((uint32_t)(q[3] & 0xFF) << 24);
-                        hi = (q[4] & 0xFF) | ((q[5] & 0xFF) << 8) | ((q[6] & 0xFF) << 16) | ((uint32_t)(q[7] & 0xFF) << 24);
-                        *reinterpret_cast<uint2*>(xrow + k0) = make_uint2(lo, hi);
-                    }
-                }
-                for (int o = 1; o < lpg; o <<= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
-                if (on && (t & (lpg - 1)) == 0) {
-                    const int g = t / lpg;
-                    xs[b * ng + g] = sc;
-                    xsum[b * ng + g] = qs;
-                }
-            }
+        }
+    }
+}
+
+// Cluster exchange: copy the other CTAs' slices of the staged activation
+// (int8 values, group scales and sums) from their shared memory into this
+// CTA's, at the same offsets.  Each slice is groups [p*ng/cs, (p+1)*ng/cs) of
+// every row; INT4 rows are two planes of n/2 bytes (even / odd values).
+template <int KIND>
+__device__ void gather_slices(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum, int ctid, int nt, int rank,
+                              int cs) {
+    const int n = a.cols, gs = a.gs, ng = n / gs;
+    for (int p = 0; p < cs; ++p) {
+        if (p == rank) continue;
+        const int pg0 = p * ng / cs, pg1 = (p + 1) * ng / cs, sg = pg1 - pg0;
+        const int half = KIND == 8 ? sg * gs / 16 : sg * gs / 32;  // 16-byte units per plane
+        const int upr = KIND == 8 ? half : 2 * half;
+        const uint32_t rx = cluster_map(xsm, p);
+        for (int i = ctid; i < a.nb * upr; i += nt) {
+            const int b = i / upr, k = i - b * upr;
+            const int off = KIND == 8 ? b * n + pg0 * gs + 16 * k
+                                      : b * n + (k < half ? 0 : n / 2) + pg0 * gs / 2 + 16 * (k < half ? k : k - half);
+            *reinterpret_cast<uint4*>(xsm + off) = ld_cluster_v4(rx + off);
+        }
+        const uint32_t rs = cluster_map(xs, p), rq = cluster_map(xsum, p);
+        for (int i = ctid; i < a.nb * sg; i += nt) {
+            const int g = (i / sg) * ng + pg0 + i % sg;
+            xs[g] = __uint_as_float(ld_cluster_u32(rs + 4 * g));
+            xsum[g] = (int)ld_cluster_u32(rq + 4 * g);
         }
     }
 }
@@ -354,7 +427,12 @@ __device__ __forceinline__ void block_dot(const uint8_t* const* rows, const floa
     }
 }
 
-// epilogue (rope_pair, finish_rows): lq_epilogue.cuh
+// epilogue (rope_pair, finish_rows): lq_epilogue.cuh.  Called out of line
+// (by one lane per row pair), so the kernels hold one copy of its cases.
+__device__ __noinline__ void finish_rows_call(const GemvArgs& a, const GemvSeg& g, int b, int r, float v0, float v1,
+                                              float u0, float u1, bool has2) {
+    finish_rows(a, g, b, r, v0, v1, u0, u1, has2);
+}
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -388,6 +466,7 @@ template <int KIND, int NB, int CPG>
 __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 4 : (NB == 2 ? 2 : 1)) gemv_kernel(const __grid_constant__ GemvArgs a, int prefetch) {
     extern __shared__ __align__(128) uint8_t smem[];
     pdl_trigger();
+    kt_start(a.kt);
     const Layout L = make_layout(a);
     float* red = reinterpret_cast<float*>(smem + L.off_red);
     int8_t* xsm = reinterpret_cast<int8_t*>(smem + L.off_x);
@@ -415,7 +494,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 4 : (NB == 2 ? 2 : 1))
         }
     }
     pdl_wait();
-    stage_input<KIND>(a, xsm, xs, xsum, red, threadIdx.x, blockDim.x);
+    kt_waited(a.kt);
+    stage_input<KIND>(a, xsm, xs, xsum, red, threadIdx.x, blockDim.x, 0, ng);
     __syncthreads();
 
     constexpr int NR = CPG >= 4 ? 2 : 4;  // rows loaded together: 8 x 16 B per lane in flight (CPG <= 4)
@@ -492,12 +572,13 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 4 : (NB == 2 ? 2 : 1))
         if (lane == 0) {
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
-                finish_rows(a, g, b, r, v[0][b], v[1][b], u[0][b], u[1][b], has2);
-                if (second) finish_rows(a, g, b, r + 2, v[2 % NR][b], v[3 % NR][b], 0.0f, 0.0f, true);
+                finish_rows_call(a, g, b, r, v[0][b], v[1][b], u[0][b], u[1][b], has2);
+                if (second) finish_rows_call(a, g, b, r + 2, v[2 % NR][b], v[3 % NR][b], 0.0f, 0.0f, true);
             }
         }
         p += npairs;
     }
+    kt_end_cta(a.kt);
 }
 
 // ---------------------------------------------------------------------------
@@ -559,7 +640,7 @@ __device__ __forceinline__ bool titem_next(const GemvArgs& a, TIter& it, int rb,
     return true;
 }
 
-__device__ __forceinline__ void titem_issue(const GemvArgs& a, const TItem& it, uint8_t* slot, uint64_t* bar, int rb,
+__device__ __noinline__ void titem_issue(const GemvArgs& a, const TItem& it, uint8_t* slot, uint64_t* bar, int rb,
                                             int ng, int gb, int tw, uint64_t pol) {
     const GemvSeg& g = a.seg[it.seg];
     const int mult = a.paired ? 2 : 1;
@@ -714,6 +795,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
     uint8_t* slots = smem + L.off_stage + (size_t)warp * 2 * L.stage_bytes;
     uint64_t* tr = a.trace ? a.trace + (size_t)blockIdx.x * 4 : nullptr;
     if (tr && threadIdx.x == 0) tr[0] = globaltimer();
+    kt_start(a.kt);
 
     if (lane == 0) {
         mbar_init(&bar[0], 1);
@@ -724,14 +806,28 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
     uint64_t pol = 0;
     TItem it;
     if (lane == 0) {
+        // `prefetch` of the warp's two first items are requested before the
+        // wait for the previous kernel, the rest after it
         pol = l2_evict_first_policy();
-        if (!prefetch) pdl_wait();
-        for (int s = 0; s < 2 && titem_next(a, iss, rb, it); ++s)
+        for (int s = 0; s < 2 && titem_next(a, iss, rb, it); ++s) {
+            if (s == prefetch) pdl_wait();
             titem_issue(a, it, slots + (size_t)s * L.stage_bytes, &bar[s], rb, ng, gb, tw, pol);
+        }
     }
     pdl_wait();
+    kt_waited(a.kt);
     if (tr && threadIdx.x == 0) tr[1] = globaltimer();
-    stage_input<KIND>(a, xsm, xs, xsum, red, threadIdx.x, blockDim.x);
+    // In a cluster each CTA builds one slice of the activation and reads the
+    // others from its peers' shared memory (the activation is read from L2 by
+    // every cluster once, not by every CTA).
+    const int cs = (int)cluster_size(), crank = (int)cluster_rank();
+    stage_input<KIND>(a, xsm, xs, xsum, red, threadIdx.x, blockDim.x, crank * ng / cs, (crank + 1) * ng / cs);
+    if (cs > 1) {
+        cluster_arrive();  // this CTA's slice is written ...
+        cluster_wait();    // ... and so is every peer's
+        gather_slices<KIND>(a, xsm, xs, xsum, threadIdx.x, blockDim.x, crank, cs);
+        cluster_arrive();  // done reading the peers (each waits for this before it exits)
+    }
     __syncthreads();
     if (tr && threadIdx.x == 0) tr[2] = globaltimer();
     // every lane walks the issue iterator too (lane 0 already advanced it)
@@ -744,10 +840,11 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
     for (int b = 0; b < NB; ++b) acc[0][b] = acc[1][b] = acc2[0][b] = acc2[1][b] = 0.0f;
     for (int k = 0; titem_next(a, cmp, rb, it); ++k) {
         const int s = k & 1;
-        if (!mbar_wait(&bar[s], (k >> 1) & 1, a.err, DEV_TIMEOUT_FULL)) {
-            // give up: confirm the copy of the other slot too, then leave
+        if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (k >> 1) & 1, a.err, DEV_TIMEOUT_FULL))) {
+            // give up: confirm the copy of the other slot too, then leave the
+            // loop (the CTA still takes its part in the cluster's last barrier)
             if (lane == 0) mbar_wait(&bar[s ^ 1], ((k + 1) >> 1) & 1, a.err, DEV_TIMEOUT_DRAIN);
-            return;
+            break;
         }
         const uint8_t* sw = slots + (size_t)s * L.stage_bytes;
         const float* ss = reinterpret_cast<const float*>(sw + kSlotW);
@@ -772,12 +869,13 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
                     smem_rows_dot<KIND, NB, CPG, 2>(wr, sr, 0, ng, xsm, xs, xsum, n, ng, lane, v);
                 }
 #pragma unroll
-                for (int q = 0; q < 4; ++q)
+                for (int q = 0; q < (PAIRED ? 4 : 2); ++q)
 #pragma unroll
                     for (int b = 0; b < NB; ++b) v[q][b] = warp_sum(v[q][b]);
                 if (lane == 0) {
-#pragma unroll
-                    for (int b = 0; b < NB; ++b) finish_rows(a, g, b, it.row + r, v[0][b], v[1][b], v[2][b], v[3][b], true);
+#pragma unroll 1
+                    for (int b = 0; b < NB; ++b)
+                        finish_rows_call(a, g, b, it.row + r, v[0][b], v[1][b], v[2][b], v[3][b], true);
                 }
             }
         } else {
@@ -812,9 +910,9 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
 #pragma unroll
                 for (int b = 0; b < NB; ++b) {
                     const float v0 = warp_sum(acc[0][b]), v1 = warp_sum(acc[1][b]);
-                    const float u0 = warp_sum(acc2[0][b]), u1 = warp_sum(acc2[1][b]);
+                    const float u0 = PAIRED ? warp_sum(acc2[0][b]) : 0.0f, u1 = PAIRED ? warp_sum(acc2[1][b]) : 0.0f;
                     acc[0][b] = acc[1][b] = acc2[0][b] = acc2[1][b] = 0.0f;
-                    if (lane == 0) finish_rows(a, g, b, it.row, v0, v1, u0, u1, true);
+                    if (lane == 0) finish_rows_call(a, g, b, it.row, v0, v1, u0, u1, true);
                 }
             }
         }
@@ -827,6 +925,8 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
             titem_issue(a, nx, slots + (size_t)s * L.stage_bytes, &bar[s], rb, ng, gb, tw, pol);
         }
     }
+    kt_end_cta(a.kt);
+    if (cs > 1) cluster_wait();  // no peer reads this CTA's shared memory any more
     if (tr) {
         __syncthreads();
         if (threadIdx.x == 0) tr[3] = globaltimer();
@@ -837,8 +937,6 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
 // stand-alone activation quantization (one pass, many CTAs): each thread
 // takes 8 consecutive values, gs/8 lanes form a group; rmsnorm CTAs each
 // compute the full sum of squares in the same fixed order.
-
-constexpr int kAqThreads = 256;
 
 // One task = 8 consecutive values of activation row b (gs/8 consecutive
 // tasks, inside one warp, form a quantization group): optional rmsnorm
@@ -892,7 +990,9 @@ __device__ __forceinline__ void quant_task8(const ActQuantArgs& a, int b, int ta
 __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_constant__ ActQuantArgs a) {
     __shared__ float red[kAqThreads / 32];
     pdl_trigger();
+    kt_start(a.kt);
     pdl_wait();
+    kt_waited(a.kt);
     const int b = blockIdx.y, n = a.n, gs = a.gs, ng = n / gs;
     const int ctid = threadIdx.x;
     const float* src = a.x ? a.x + (size_t)b * n : nullptr;
@@ -960,6 +1060,7 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_cons
         }
     }
     quant_task8(a, b, task, on, norm, inv, v);
+    kt_end_cta(a.kt);
 }
 
 cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl) {
@@ -989,7 +1090,9 @@ __global__ void __launch_bounds__(1024) peer_add_quant_kernel(const __grid_const
     __shared__ uint32_t s_call;
     const ActQuantArgs& a = pa.q;
     pdl_trigger();
+    kt_start(a.kt);
     pdl_wait();  // this process's partial (the previous kernel's output) is complete
+    kt_waited(a.kt);
     const int b = blockIdx.y, n = a.n, ctid = threadIdx.x;
     if (ctid == 0) {
         const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(&pa.counters[0]) + 1u;
@@ -1087,6 +1190,7 @@ __global__ void __launch_bounds__(1024) peer_add_quant_kernel(const __grid_const
     for (int w = 0; w < kAqThreads / 32; ++w) t += red[w];
     const float inv = 1.0f / sqrtf(t / (float)n + 1e-5f);
     quant_task8(a, b, task, on, true, inv, v);
+    kt_end_cta(a.kt);
 }
 
 cudaError_t peer_add_quant_launch(const PeerAddArgs& a, cudaStream_t st, bool pdl) {
@@ -1117,8 +1221,7 @@ static bool gs_ok(int gs) { return gs_ok_dev(gs); }
 
 bool gemv_args_ok(const GemvArgs& a, int kind) {
     if (!gs_ok(a.gs) || a.cols % a.gs || a.nseg < 1 || a.nseg > kMaxSegs) return false;
-    // the rmsnorm prologue holds the whole input in registers: 8 values x 8 rounds x 256 threads
-    if ((a.in_mode == IN_RMSNORM || a.in_mode == IN_RMSNORM_EMB) && a.cols > 8 * 8 * kCT) return false;
+    if (a.cols % 8) return false;
     for (int i = 0; i < a.nseg; ++i) {
         if (!aligned16(a.seg[i].wq)) return false;
         if (a.paired && !aligned16(a.seg[i].wq2)) return false;
@@ -1137,6 +1240,50 @@ static bool tma_ok(const GemvArgs& a) {
 }
 
 static int g_use_tma = -1;
+
+// Shared-memory budget per bulk-copy GEMV CTA: two CTAs (of consecutive
+// kernels) fit one SM's 228 KB with 1 KB reserved each.  LQ_GEMV_SMEM_KB
+// overrides it (for tuning).
+// Weight items (of two) each warp requests before the wait for the previous
+// kernel, and the most warps per CTA (tuning: LQ_GEMV_PREFETCH, LQ_GEMV_MAXWARPS).
+static int gemv_prefetch_items() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("LQ_GEMV_PREFETCH");
+        v = e ? atoi(e) : 2;
+        if (v < 0 || v > 2) v = 2;
+    }
+    return v;
+}
+// CTAs per cluster sharing the activation staging (1, 2 or 4; LQ_GEMV_CLUSTER)
+static int gemv_cluster() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("LQ_GEMV_CLUSTER");
+        v = e ? atoi(e) : 1;
+        if (v != 1 && v != 2 && v != 4) v = 1;
+    }
+    return v;
+}
+static int gemv_max_warps() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("LQ_GEMV_MAXWARPS");
+        v = e ? atoi(e) : kTmaMaxWarps;
+        if (v < 4 || v > kTmaMaxWarps) v = kTmaMaxWarps;
+    }
+    return v;
+}
+
+static int gemv_smem_target() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("LQ_GEMV_SMEM_KB");
+        v = (e ? atoi(e) : 227) * 1024;
+        if (v < 32 * 1024 || v > 227 * 1024) v = 227 * 1024;
+    }
+    return v;
+}
 
 template <int KIND, int NB, int CPG>
 static cudaError_t launch_tma(GemvArgs a, cudaStream_t st, bool pdl, int num_sms) {
@@ -1161,9 +1308,17 @@ static cudaError_t launch_tma(GemvArgs a, cudaStream_t st, bool pdl, int num_sms
     int P = 0;
     for (int i = 0; i < a.nseg; ++i) P += a.seg[i].rows / 2;
     if (P == 0) return cudaSuccess;
-    // as many warps (two slots each) as shared memory holds, up to 16
+    // Warps (two slots each): as many as fit half an SM's shared memory, so
+    // that the next kernel's CTA can be resident beside this one and stream
+    // its first weights while this one finishes; at least four warps, else as
+    // many as fit the whole SM (up to 16).
     int nw = 0;
-    for (int w = kTmaMaxWarps; w >= 4 && !nw; w -= 2) {
+    const int wmax = gemv_max_warps();
+    for (int w = wmax; w >= 4 && !nw; --w) {
+        a.nstages = 2 * w;
+        if (make_layout(a).total <= gemv_smem_target()) nw = w;
+    }
+    for (int w = wmax; w >= 4 && !nw; --w) {
         a.nstages = 2 * w;
         if (make_layout(a).total <= 227 * 1024) nw = w;
     }
@@ -1180,19 +1335,43 @@ static cudaError_t launch_tma(GemvArgs a, cudaStream_t st, bool pdl, int num_sms
         if (e != cudaSuccess) return e;
         attr_set[a.split][a.paired] = true;
     }
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     int grid = (P + nw - 1) / nw;
     if (grid > num_sms) grid = num_sms;
+    // clusters of cs CTAs share the activation staging (grid a multiple of cs,
+    // and no larger than the clusters that can be resident at once)
+    int cs = gemv_cluster();
+    if (cs > 1 && (grid < cs || ng < cs)) cs = 1;
+    if (cs > 1) grid = grid / cs * cs;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    if (cs > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = cs;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(nw * 32);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = st;
     cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, a, pdl ? 1 : 0);
+    cfg.numAttrs = na;
+    if (cs > 1) {
+        int mc = 0;
+        if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) == cudaSuccess && mc >= 1 && mc * cs < grid) {
+            grid = mc * cs;
+            cfg.gridDim = dim3(grid);
+        }
+        cudaGetLastError();
+    }
+    return cudaLaunchKernelEx(&cfg, kern, a, pdl ? gemv_prefetch_items() : 0);
 }
 
 template <int KIND, int NB, int CPG>

@@ -27,6 +27,8 @@ int cuda_fail(cudaError_t e, const char* what);
 int check_device_error(int* err_dev, cudaStream_t st);
 int noalloc_check_error(cudaStream_t st);  // matmul_f32_noalloc's error word (noalloc.cu)
 cudaStream_t stream();
+int launch_flags();     // lq_set_launch_flags
+uint64_t* trace_buffer();  // lq_set_trace
 int matmul_f32_device(float* yd, const float* xd, const QuantizedTensor* w, int n, int d, int8_t* xq, float* xs,
                       int* xsum, int* err, cudaStream_t st, bool pdl_first, int num_sms, uint64_t* trace);
 

@@ -66,6 +66,7 @@ struct GemvArgs {
     int64_t kv_seq_stride;  // elements between sequences' caches
     int* err;
     uint64_t* trace;  // optional per-CTA phase timestamps (globaltimer ns), [grid][4]; null = off
+    uint64_t* kt;     // optional step-trace stamps of this launch (lq_device.cuh kt_*); null = off
     // schedule (filled by the planner)
     int split;       // 0: stages of whole rows; 1: stages are slices of one row
     int stage_rows;  // rows per stage (whole-row mode)
@@ -114,6 +115,7 @@ struct ActQuantArgs {
     float* xs_t;
     int xs_nfull, xs_npad_last;
     float xs_t_mul;
+    uint64_t* kt;      // optional step-trace stamps of this launch; null = off
 };
 cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl);
 

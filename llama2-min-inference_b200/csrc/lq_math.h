@@ -7,7 +7,8 @@
  * Only IEEE +, *, fma and rint are used, in a fixed order, so the CPU and the
  * GPU produce the same bits (build the device code with --fmad=false and the
  * host code with -ffp-contract=off).  Accuracy: within 2 ulp of the true
- * value (checked against libm in tests/test_math.py).
+ * value (tests/test_math.py compares it with float64 exp over every 97th
+ * float of [-104, 88.7]: at most 0.92 ulp).
  */
 #ifndef LQ_MATH_H
 #define LQ_MATH_H

@@ -14,7 +14,10 @@ struct QW {
 };
 
 int forward_launch(Transformer* t, int batch);
+// the next kernel's step-trace stamps (null when tracing is off); records its kind
+uint64_t* kt_next(Transformer* t, int kind);
 int run_step(Transformer* t, const int* tokens, const int* pos, int batch, bool want_logits, bool want_next);
+int run_prompt(Transformer* t, const int* tokens, int n, int start);
 int kernels_per_step(const Transformer* t, int batch);
 
 }  // namespace lq
@@ -63,6 +66,16 @@ struct Transformer {
     // pinned host mirrors
     float* h_logits = nullptr;
     int *h_meta = nullptr, *h_next = nullptr, *h_err = nullptr;
+    // step trace (transformer_trace): three stamps per kernel of the step and the kernels' kinds
+    uint64_t* ktr = nullptr;
+    int ktr_cap = 0, ktr_n = 0;
+    int* ktr_kind = nullptr;
+    // prompt steps (forward_prompt): every row is a position of sequence
+    // prompt_seq (-1 while capturing the decode step); their own graph
+    int prompt_seq = -1;
+    cudaGraph_t pgraph = nullptr;
+    cudaGraphExec_t pexec = nullptr;
+    int pgraph_rows = 0;
     // graph
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t exec = nullptr;

@@ -21,6 +21,7 @@ struct AttnArgs {
     int64_t kv_seq_stride;
     int q_stride;
     int n_heads, n_kv_heads, kv_mul, head_size, max_seq, max_splits;
+    uint64_t* kt;        // optional step-trace stamps of this launch; null = off
 };
 
 cudaError_t quantize_act_launch(const float* x, int64_t rows, int64_t n, int gs, int8_t* xq, float* xs,
@@ -28,7 +29,7 @@ cudaError_t quantize_act_launch(const float* x, int64_t rows, int64_t n, int gs,
 size_t attention_smem_bytes(int head_size, int kv_mul);
 cudaError_t attention_launch(const AttnArgs& a, int batch, cudaStream_t st, bool pdl);
 cudaError_t argmax_launch(const float* logits, int n, int batch, int stride, int* out, cudaStream_t st,
-                          bool pdl);
+                          bool pdl, uint64_t* kt = nullptr);
 cudaError_t synth_f32_launch(float* out, int64_t n, uint64_t seed, int tid, float std, int ones,
                              cudaStream_t st);
 cudaError_t synth_quant_launch(uint8_t* q, float* s, int64_t rows, int64_t cols, int gs, int kind,

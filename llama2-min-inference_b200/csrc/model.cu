@@ -29,6 +29,7 @@
 #include <vector>
 
 #include "lq_ctx.h"
+#include "lq_device.cuh"  // kKtSlots (step-trace layout)
 #include "lq_host.h"
 #include "lq_kernels.h"
 #include "lq_model.h"
@@ -76,6 +77,7 @@ const Nccl* nccl() {
 }
 
 constexpr int kQgTiles = 8192;  // arrival counters: tiles of the largest launch (vocab / 128)
+constexpr int kPromptRows = 64;  // prompt tokens per prefill step (forward_prompt)
 
 int alloc_q(QW& w, int64_t rows, int64_t cols, int gs, int kind) {
     w.rows = rows;
@@ -135,10 +137,12 @@ int check_config(const Config* c, int gs, int tp_size = 1) {
     return LQ_OK;
 }
 
-// device state sized for max_batch sequences
+// device state: KV caches for max_batch sequences; activations for
+// max(max_batch, kPromptRows) rows (a prompt chunk is up to kPromptRows rows
+// of one sequence)
 int alloc_state(Transformer* t) {
     const Config& c = t->c;
-    const int B = t->max_batch;
+    const int B = t->max_batch > kPromptRows ? t->max_batch : kPromptRows;  // activation rows
     t->head_size = c.dim / c.n_heads;
     t->kv_mul = c.n_heads / c.n_kv_heads;
     t->nh_l = c.n_heads / t->tp_size;
@@ -147,7 +151,7 @@ int alloc_state(Transformer* t) {
     t->kv_dim = t->nkv_l * t->head_size;  // this process's kv width
     t->hid_l = c.hidden_dim / t->tp_size;
     t->max_splits = (t->max_seq + kChunk - 1) / kChunk;
-    const size_t kv = (size_t)B * c.n_layers * t->kv_dim * t->max_seq;
+    const size_t kv = (size_t)t->max_batch * c.n_layers * t->kv_dim * t->max_seq;
     int rc = LQ_OK;
     rc = rc ? rc : dalloc(&t->x, (size_t)B * c.dim);
     rc = rc ? rc : dalloc(&t->q, (size_t)B * t->dq_l);
@@ -221,6 +225,11 @@ void free_state(Transformer* t) {
     t->exec = nullptr;
     t->graph = nullptr;
     t->graph_batch = 0;
+    if (t->pexec) cudaGraphExecDestroy(t->pexec);
+    if (t->pgraph) cudaGraphDestroy(t->pgraph);
+    t->pexec = nullptr;
+    t->pgraph = nullptr;
+    t->pgraph_rows = 0;
     void* bufs[] = {t->x, t->q, t->att, t->h1, t->h3, t->xq, t->xqs, t->xqsum, t->logits, t->kc, t->vc,
                     t->part, t->counters, t->meta, t->next, t->err, t->rope, t->xs_t, t->qg_part, t->qg_cnt,
                     t->x2, t->ybuf};
@@ -250,7 +259,7 @@ int gemv_chunk(int cols) {
 
 // One GEMV over `batch` activation rows: launches of up to gemv_chunk rows,
 // the last one rounded up to a kernel row count with the extra rows unstored.
-cudaError_t gemv_rows(const GemvArgs& a, int kind, int batch, cudaStream_t st, int num_sms);
+cudaError_t gemv_rows(Transformer* t, const GemvArgs& a, int kind, int batch, cudaStream_t st);
 
 // The product of one decode stage for `batch` activation rows: from
 // t->mma_min rows on, on the tensor cores (up to 64 rows per launch), else
@@ -272,16 +281,17 @@ cudaError_t product_rows(Transformer* t, const GemvArgs& a, int batch, cudaStrea
             if (c.kcache) c.kcache += (size_t)b0 * a.kv_seq_stride;
             if (c.vcache) c.vcache += (size_t)b0 * a.kv_seq_stride;
             // this chunk's scale table: [ng][npad] at chunk offset ng * 64
+            c.kt = kt_next(t, LQ_TRACE_QGEMM);
             cudaError_t e = qgemm_launch(c, kind, t->xs_t + (size_t)(b0 / 64) * ng * 64, qgemm_npad(rows), t->qg_part,
                                          t->qg_cnt, st, true, t->num_sms);
             if (e != cudaSuccess) return e;
         }
         return cudaSuccess;
     }
-    return gemv_rows(a, kind, batch, st, t->num_sms);
+    return gemv_rows(t, a, kind, batch, st);
 }
 
-cudaError_t gemv_rows(const GemvArgs& a, int kind, int batch, cudaStream_t st, int num_sms) {
+cudaError_t gemv_rows(Transformer* t, const GemvArgs& a, int kind, int batch, cudaStream_t st) {
     const int chunk = gemv_chunk(a.cols);
     const int ng = a.cols / a.gs;
     for (int b0 = 0; b0 < batch; b0 += chunk) {
@@ -294,12 +304,15 @@ cudaError_t gemv_rows(const GemvArgs& a, int kind, int batch, cudaStream_t st, i
         c.xq = a.xq + (size_t)b0 * a.cols;
         c.xs = a.xs + (size_t)b0 * ng;
         c.xsum_in = a.xsum_in ? a.xsum_in + (size_t)b0 * ng : nullptr;
+        if (c.xf) c.xf = a.xf + (size_t)b0 * a.cols;
+        if (c.x_out) c.x_out = a.x_out + (size_t)b0 * a.cols;
         c.meta = a.meta + 2 * b0;
         for (int i = 0; i < c.nseg; ++i)
             if (c.seg[i].y) c.seg[i].y += (size_t)b0 * a.y_stride;
         if (c.kcache) c.kcache += (size_t)b0 * a.kv_seq_stride;
         if (c.vcache) c.vcache += (size_t)b0 * a.kv_seq_stride;
-        cudaError_t e = gemv_launch(c, kind, st, true, num_sms);
+        c.kt = kt_next(t, LQ_TRACE_GEMV);
+        cudaError_t e = gemv_launch(c, kind, st, true, t->num_sms);
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
@@ -325,8 +338,114 @@ Transformer* new_transformer(const Config* c, int kind, int gs, int max_seq, int
 
 namespace lq {
 
+uint64_t* kt_next(Transformer* t, int kind) {
+    if (!t->ktr || t->ktr_n >= t->ktr_cap) return nullptr;
+    t->ktr_kind[t->ktr_n] = kind;
+    return t->ktr + 3 * kKtSlots * (size_t)t->ktr_n++;
+}
+
+// The decode step for 1..mma_min-1 sequences on one GPU: five kernels per
+// layer.  Every GEMV builds its int8 activation in its own prologue (rmsnorm
+// + quantize_act, or quantize_act of the fp32 input, with the stand-alone
+// quantizer's arithmetic), so no quantizer kernel sits between the products:
+//   GEMV [wq|wk|wv]  prologue rmsnorm(x) (layer 0: x = emb[token])  epilogue RoPE / K, V cache
+//   attention
+//   GEMV wo          prologue quantize(att)                          epilogue x += .
+//   GEMV [w1|w3]     prologue rmsnorm(x)                             epilogue SwiGLU
+//   GEMV w2          prologue quantize(h)                            epilogue x += .
+// then the classifier GEMV (prologue: final rmsnorm) and argmax.
+template <typename Base>
+static int forward_fused(Transformer* t, int batch, Base& base) {
+    const Config& c = t->c;
+    const int kind = t->kind;
+    const int D = c.dim, DQ = t->dq_l, H = t->hid_l, KV = t->kv_dim, hs = t->head_size, gs = t->gs;
+    const int64_t rbD = rbytes(D, kind), rbQ = rbytes(DQ, kind), rbH = rbytes(H, kind);
+    const int ngD = D / gs, ngQ = DQ / gs, ngH = H / gs;
+    const int64_t kv_layer = (int64_t)t->nkv_l * t->max_seq * hs;
+    // decode: row b is sequence b (its own cache); prompt: every row is a
+    // position of sequence prompt_seq (one cache, no stride between rows)
+    const int64_t kv_seq = t->prompt_seq >= 0 ? 0 : (int64_t)c.n_layers * kv_layer;
+    float* const kc = t->kc + (t->prompt_seq >= 0 ? (int64_t)t->prompt_seq * c.n_layers * kv_layer : 0);
+    float* const vc = t->vc + (t->prompt_seq >= 0 ? (int64_t)t->prompt_seq * c.n_layers * kv_layer : 0);
+    cudaStream_t st = t->stream;
+    cudaError_t e;
+    float* x = t->x;
+    for (int l = 0; l < c.n_layers; ++l) {
+        GemvArgs a;
+        base(a, D);
+        a.seg[0] = {t->wq.q + (size_t)l * DQ * rbD, t->wq.s + (size_t)l * DQ * ngD, t->q, DQ, EPI_ROPE_Q};
+        a.seg[1] = {t->wk.q + (size_t)l * KV * rbD, t->wk.s + (size_t)l * KV * ngD, nullptr, KV, EPI_ROPE_KCACHE};
+        a.seg[2] = {t->wv.q + (size_t)l * KV * rbD, t->wv.s + (size_t)l * KV * ngD, nullptr, KV, EPI_VCACHE};
+        a.nseg = 3;
+        a.y_stride = DQ;
+        a.in_mode = l == 0 ? IN_RMSNORM_EMB : IN_RMSNORM;
+        a.xf = x;
+        a.rms_w = t->rms_att + (size_t)l * D;
+        a.emb = t->emb;
+        a.x_out = x;
+        a.kcache = kc + l * kv_layer;
+        a.vcache = vc + l * kv_layer;
+        if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
+        AttnArgs at{};
+        at.q = t->q;
+        at.kcache = kc + l * kv_layer;
+        at.vcache = vc + l * kv_layer;
+        at.out = t->att;
+        at.part = t->part;
+        at.counters = t->counters;
+        at.meta = t->meta;
+        at.err = t->err;
+        at.kv_seq_stride = kv_seq;
+        at.q_stride = DQ;
+        at.n_heads = t->nh_l;
+        at.n_kv_heads = t->nkv_l;
+        at.kv_mul = t->kv_mul;
+        at.head_size = hs;
+        at.max_seq = t->max_seq;
+        at.max_splits = t->max_splits;
+        at.kt = kt_next(t, LQ_TRACE_ATTENTION);
+        if ((e = attention_launch(at, batch, st, true)) != cudaSuccess) return cuda_fail(e, "attention");
+        base(a, DQ);
+        a.seg[0] = {t->wo.q + (size_t)l * D * rbQ, t->wo.s + (size_t)l * D * ngQ, x, D, EPI_ADD};
+        a.nseg = 1;
+        a.in_mode = IN_F32;
+        a.xf = t->att;
+        if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "wo gemv");
+        base(a, D);
+        a.seg[0] = {t->w1.q + (size_t)l * H * rbD, t->w1.s + (size_t)l * H * ngD, t->h1, H, EPI_SWIGLU,
+                    t->w3.q + (size_t)l * H * rbD, t->w3.s + (size_t)l * H * ngD};
+        a.nseg = 1;
+        a.paired = 1;
+        a.y_stride = H;
+        a.in_mode = IN_RMSNORM;
+        a.xf = x;
+        a.rms_w = t->rms_ffn + (size_t)l * D;
+        if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "w1/w3 gemv");
+        base(a, H);
+        a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, x, D, EPI_ADD};
+        a.nseg = 1;
+        a.in_mode = IN_F32;
+        a.xf = t->h1;
+        if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
+    }
+    GemvArgs a;
+    base(a, D);
+    a.seg[0] = {t->wcls.q, t->wcls.s, t->logits, c.vocab_size, EPI_STORE};
+    a.nseg = 1;
+    a.y_stride = c.vocab_size;
+    a.in_mode = IN_RMSNORM;
+    a.xf = x;
+    a.rms_w = t->rms_final;
+    if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "classifier gemv");
+    if ((e = argmax_launch(t->logits, c.vocab_size, batch, c.vocab_size, t->next, st, true,
+                           kt_next(t, LQ_TRACE_ARGMAX))) != cudaSuccess)
+        return cuda_fail(e, "argmax");
+    return LQ_OK;
+}
+
 // Issue one decode step for `batch` sequences on t->stream (capturable).
 int forward_launch(Transformer* t, int batch) {
+    t->ktr_n = 0;
     const Config& c = t->c;
     const int kind = t->kind, gs = t->gs;
     // local widths: the whole model on one GPU, or this process's share under tensor parallelism
@@ -334,7 +453,11 @@ int forward_launch(Transformer* t, int batch) {
     const int64_t rbD = rbytes(D, kind), rbQ = rbytes(DQ, kind), rbH = rbytes(H, kind);
     const int ngD = D / gs, ngQ = DQ / gs, ngH = H / gs;
     const int64_t kv_layer = (int64_t)t->nkv_l * t->max_seq * hs;
-    const int64_t kv_seq = (int64_t)c.n_layers * kv_layer;
+    // decode: row b is sequence b (its own cache); prompt: every row is a
+    // position of sequence prompt_seq (one cache, no stride between rows)
+    const int64_t kv_seq = t->prompt_seq >= 0 ? 0 : (int64_t)c.n_layers * kv_layer;
+    float* const kc = t->kc + (t->prompt_seq >= 0 ? (int64_t)t->prompt_seq * c.n_layers * kv_layer : 0);
+    float* const vc = t->vc + (t->prompt_seq >= 0 ? (int64_t)t->prompt_seq * c.n_layers * kv_layer : 0);
     cudaStream_t st = t->stream;
     auto base = [&](GemvArgs& a, int cols) {
         a = GemvArgs{};
@@ -373,6 +496,7 @@ int forward_launch(Transformer* t, int batch) {
             q.xs_npad_last = batch % 64 ? qgemm_npad(batch % 64) : 64;
             q.xs_t_mul = kind == LQ_KIND_INT4 ? 0.0625f : 1.0f;
         }
+        q.kt = kt_next(t, LQ_TRACE_QUANT);
         return act_quant_launch(q, st, true);
     };
     auto qin = [&](GemvArgs& a) {
@@ -386,6 +510,7 @@ int forward_launch(Transformer* t, int batch) {
     // next quantizer, which reads one residual buffer and writes the other
     auto allreduce = [&]() -> int {
         if (t->tp_size == 1 || !t->tp_nccl) return LQ_OK;
+        kt_next(t, LQ_TRACE_NCCL);  // a library kernel: kind recorded, no stamps
         const ncclResult_t r = nccl()->all_reduce(t->ybuf, t->ybuf, (size_t)batch * D, ncclFloat, ncclSum,
                                                   static_cast<ncclComm_t>(t->comm), st);
         return r == ncclSuccess ? LQ_OK : lq_fail(LQ_ECUDA, "all-reduce: %s", nccl()->error_string(r));
@@ -428,6 +553,7 @@ int forward_launch(Transformer* t, int batch) {
         p.tp_size = t->tp_size;
         p.err = t->err;
         p.wait_ns = t->tp_wait_ns;
+        p.q.kt = kt_next(t, LQ_TRACE_ALLREDUCE);
         return peer_add_quant_launch(p, st, true);
     };
     float* ywo = peer ? slot(0) : t->ybuf;  // where the partial products go
@@ -435,6 +561,12 @@ int forward_launch(Transformer* t, int batch) {
     float* xa = t->x;              // residual stream after attention's add (and the embedding)
     float* xb = t->tp ? t->x2 : t->x;  // after the ffn's add
     int rc;
+    static int fused = -1;
+    if (fused < 0) {
+        const char* e = getenv("LQ_DECODE_FUSED");
+        fused = e ? atoi(e) : 0;
+    }
+    if (fused && !t->tp && !use_mma(t, batch)) return forward_fused(t, batch, base);
     for (int l = 0; l < c.n_layers; ++l) {
         GemvArgs a;
         // 1. q, k, v (attention rmsnorm + quantize first; layer 0 starts from emb[token])
@@ -453,14 +585,14 @@ int forward_launch(Transformer* t, int batch) {
         a.nseg = 3;
         a.y_stride = DQ;
         qin(a);
-        a.kcache = t->kc + l * kv_layer;
-        a.vcache = t->vc + l * kv_layer;
+        a.kcache = kc + l * kv_layer;
+        a.vcache = vc + l * kv_layer;
         if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
         // 2. attention (this process's heads)
         AttnArgs at{};
         at.q = t->q;
-        at.kcache = t->kc + l * kv_layer;
-        at.vcache = t->vc + l * kv_layer;
+        at.kcache = kc + l * kv_layer;
+        at.vcache = vc + l * kv_layer;
         at.out = t->att;
         at.part = t->part;
         at.counters = t->counters;
@@ -474,6 +606,7 @@ int forward_launch(Transformer* t, int batch) {
         at.head_size = hs;
         at.max_seq = t->max_seq;
         at.max_splits = t->max_splits;
+        at.kt = kt_next(t, LQ_TRACE_ATTENTION);
         if ((e = attention_launch(at, batch, st, true)) != cudaSuccess) return cuda_fail(e, "attention");
         // 3. wo + residual
         if ((e = quant(IN_F32, t->att, DQ, nullptr)) != cudaSuccess) return cuda_fail(e, "attention output quantize");
@@ -515,7 +648,8 @@ int forward_launch(Transformer* t, int batch) {
     a.y_stride = c.vocab_size;
     qin(a);
     if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "classifier gemv");
-    if ((e = argmax_launch(t->logits, c.vocab_size, batch, c.vocab_size, t->next, st, true)) != cudaSuccess)
+    if ((e = argmax_launch(t->logits, c.vocab_size, batch, c.vocab_size, t->next, st, true,
+                           kt_next(t, LQ_TRACE_ARGMAX))) != cudaSuccess)
         return cuda_fail(e, "argmax");
     return LQ_OK;
 }
@@ -525,10 +659,13 @@ int kernels_per_step(const Transformer* t, int batch) {
         const int g = (batch + 63) / 64;
         return t->c.n_layers * (5 + 4 * g) + 2 + g;
     }
-    const int cd = gemv_chunk(t->c.dim), ch = gemv_chunk(t->c.hidden_dim);
-    const int gd = (batch + cd - 1) / cd, gh = (batch + ch - 1) / ch;
-    // per layer: 4 quantizers, attention, GEMVs qkv / wo / w1|w3 (dim inputs) and w2 (hidden inputs)
-    return t->c.n_layers * (5 + 3 * gd + gh) + 2 + gd;
+    const int cd = gemv_chunk(t->c.dim), ch = gemv_chunk(t->hid_l), cq = gemv_chunk(t->dq_l);
+    const int gd = (batch + cd - 1) / cd, gh = (batch + ch - 1) / ch, gq = (batch + cq - 1) / cq;
+    if (t->tp || !getenv("LQ_DECODE_FUSED") || atoi(getenv("LQ_DECODE_FUSED")) == 0)
+        // per layer: 4 quantizers, attention, GEMVs qkv / wo / w1|w3 / w2
+        return t->c.n_layers * (5 + 2 * gd + gq + gh) + 2 + gd;
+    // per layer: attention and the GEMVs qkv / wo / w1|w3 / w2, each quantizing its own input
+    return t->c.n_layers * (1 + 2 * gd + gq + gh) + 1 + gd;
 }
 
 static int ensure_graph(Transformer* t, int batch) {
@@ -558,6 +695,71 @@ static int ensure_graph(Transformer* t, int batch) {
     return LQ_OK;
 }
 
+// The prompt step's graph for `rows` rows (every row a position of sequence 0).
+static int ensure_prompt_graph(Transformer* t, int rows) {
+    if (t->pexec && t->pgraph_rows == rows) return LQ_OK;
+    if (t->pexec) cudaGraphExecDestroy(t->pexec);
+    if (t->pgraph) cudaGraphDestroy(t->pgraph);
+    t->pexec = nullptr;
+    t->pgraph = nullptr;
+    t->pgraph_rows = 0;
+    cudaError_t e = cudaStreamBeginCapture(t->stream, cudaStreamCaptureModeThreadLocal);
+    if (e != cudaSuccess) return cuda_fail(e, "begin capture");
+    t->prompt_seq = 0;
+    int rc = forward_launch(t, rows);
+    t->prompt_seq = -1;
+    cudaGraph_t g = nullptr;
+    e = cudaStreamEndCapture(t->stream, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "end capture");
+    t->pgraph = g;
+    e = cudaGraphInstantiate(&t->pexec, g, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "graph instantiate");
+    t->pgraph_rows = rows;
+    return LQ_OK;
+}
+
+// Prompt prefill: tokens[0..n) at positions start..start+n-1 of sequence 0,
+// in steps of up to kPromptRows rows; the last token's logits go to h_logits.
+int run_prompt(Transformer* t, const int* tokens, int n, int start) {
+    if (!t->x) return lq_fail(LQ_EINVAL, "model has no decode state (a failed transformer_reserve_batch)");
+    if (n < 1 || start < 0 || (int64_t)start + n > t->max_seq)
+        return lq_fail(LQ_EINVAL, "prompt of %d tokens at position %d does not fit the %d positions", n, start,
+                       t->max_seq);
+    for (int i = 0; i < n; ++i)
+        if (tokens[i] < 0 || tokens[i] >= t->c.vocab_size)
+            return lq_fail(LQ_EINVAL, "token %d out of range [0, %d)", tokens[i], t->c.vocab_size);
+    cudaStream_t st = t->stream;
+    for (int done = 0; done < n;) {
+        const int rows = n - done < kPromptRows ? n - done : kPromptRows;
+        for (int b = 0; b < rows; ++b) {
+            t->h_meta[2 * b] = tokens[done + b];
+            t->h_meta[2 * b + 1] = start + done + b;
+        }
+        int rc = ensure_prompt_graph(t, rows);
+        if (rc) return rc;
+        cudaError_t e = cudaMemcpyAsync(t->meta, t->h_meta, 2 * rows * sizeof(int), cudaMemcpyHostToDevice, st);
+        if (e == cudaSuccess) e = cudaGraphLaunch(t->pexec, st);
+        done += rows;
+        if (e == cudaSuccess && done == n)
+            e = cudaMemcpyAsync(t->h_logits, t->logits + (size_t)(rows - 1) * t->c.vocab_size,
+                                (size_t)t->c.vocab_size * sizeof(float), cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaMemcpyAsync(t->h_err, t->err, sizeof(int), cudaMemcpyDeviceToHost, st);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+        if (e != cudaSuccess) return cuda_fail(e, "prompt step");
+        if (t->h_err[0] != 0) {
+            const int code = t->h_err[0];
+            cudaMemsetAsync(t->err, 0, sizeof(int), st);
+            cudaStreamSynchronize(st);
+            return lq_fail(LQ_ETIMEOUT, "device-side wait gave up in a prompt step (code 0x%x)", code);
+        }
+    }
+    return LQ_OK;
+}
+
 // One step for `batch` sequences: H2D tokens/positions, graph, optional D2H.
 int run_step(Transformer* t, const int* tokens, const int* pos, int batch, bool want_logits, bool want_next) {
     if (!t->x) return lq_fail(LQ_EINVAL, "model has no decode state (a failed transformer_reserve_batch)");
@@ -575,6 +777,7 @@ int run_step(Transformer* t, const int* tokens, const int* pos, int batch, bool 
     if (rc) return rc;
     cudaStream_t st = t->stream;
     cudaError_t e = cudaMemcpyAsync(t->meta, t->h_meta, 2 * batch * sizeof(int), cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess && t->ktr) e = cudaMemsetAsync(t->ktr, 0xFF, 3 * kKtSlots * sizeof(uint64_t) * t->ktr_cap, st);
     if (e == cudaSuccess) e = cudaGraphLaunch(t->exec, st);
     if (e == cudaSuccess && want_logits)
         e = cudaMemcpyAsync(t->h_logits, t->logits, (size_t)batch * t->c.vocab_size * sizeof(float),
@@ -940,6 +1143,15 @@ float* forward(Transformer* t, int token, int pos) {
     return t->h_logits;
 }
 
+float* forward_prompt(Transformer* t, const int* tokens, int n_tokens, int start_pos) {
+    if (!t || !tokens) {
+        lq_fail(LQ_EINVAL, "forward_prompt: null argument");
+        return nullptr;
+    }
+    if (run_prompt(t, tokens, n_tokens, start_pos) != LQ_OK) return nullptr;
+    return t->h_logits;
+}
+
 int forward_argmax(Transformer* t, int token, int pos, int* next_token) {
     if (!t || !next_token) return lq_fail(LQ_EINVAL, "forward_argmax: null argument");
     int rc = run_step(t, &token, &pos, 1, false, true);
@@ -951,6 +1163,8 @@ int forward_argmax(Transformer* t, int token, int pos, int* next_token) {
 void free_transformer(Transformer* t) {
     if (!t) return;
     free_state(t);  // the captured graph (which holds the all-reduces) goes before the communicator
+    if (t->ktr) cudaFree(t->ktr);
+    free(t->ktr_kind);
     xr_teardown(t);
     if (t->comm && nccl()) nccl()->comm_destroy(static_cast<ncclComm_t>(t->comm));
     t->comm = nullptr;
@@ -1061,6 +1275,70 @@ int lq_tp_wait_selftest(int tp_size, int wait_us, double* first_ms, double* seco
     if (st) cudaStreamDestroy(st);
     if (buf) cudaFree(buf);
     return rc;
+}
+
+int transformer_trace(Transformer* t, int enable) {
+    if (!t) return lq_fail(LQ_EINVAL, "transformer_trace: null transformer");
+    if (t->stream) cudaStreamSynchronize(t->stream);
+    // the captured graphs hold the trace pointers: capture again at the next step
+    if (t->exec) cudaGraphExecDestroy(t->exec);
+    if (t->graph) cudaGraphDestroy(t->graph);
+    if (t->pexec) cudaGraphExecDestroy(t->pexec);
+    if (t->pgraph) cudaGraphDestroy(t->pgraph);
+    t->exec = nullptr;
+    t->graph = nullptr;
+    t->graph_batch = 0;
+    t->pexec = nullptr;
+    t->pgraph = nullptr;
+    t->pgraph_rows = 0;
+    if (t->ktr) cudaFree(t->ktr);
+    free(t->ktr_kind);
+    t->ktr = nullptr;
+    t->ktr_kind = nullptr;
+    t->ktr_cap = t->ktr_n = 0;
+    if (!enable) return LQ_OK;
+    const int cap = 16384;
+    cudaError_t e = cudaMalloc(&t->ktr, 3 * kKtSlots * sizeof(uint64_t) * cap);
+    if (e == cudaSuccess) e = cudaMemset(t->ktr, 0xFF, 3 * kKtSlots * sizeof(uint64_t) * cap);
+    t->ktr_kind = static_cast<int*>(calloc(cap, sizeof(int)));
+    if (e != cudaSuccess || !t->ktr_kind) {
+        if (t->ktr) cudaFree(t->ktr);
+        free(t->ktr_kind);
+        t->ktr = nullptr;
+        t->ktr_kind = nullptr;
+        return e != cudaSuccess ? cuda_fail(e, "transformer_trace") : lq_fail(LQ_ENOMEM, "transformer_trace");
+    }
+    t->ktr_cap = cap;
+    return LQ_OK;
+}
+
+int transformer_trace_read(Transformer* t, int max_kernels, int* kinds, uint64_t* stamps, int* count) {
+    if (!t || !count) return lq_fail(LQ_EINVAL, "transformer_trace_read: null argument");
+    if (!t->ktr) return lq_fail(LQ_EINVAL, "transformer_trace_read: tracing is off (transformer_trace)");
+    const int n = t->ktr_n < max_kernels ? t->ktr_n : max_kernels;
+    *count = t->ktr_n;
+    if (n <= 0) return LQ_OK;
+    std::vector<uint64_t> raw((size_t)3 * kKtSlots * n);
+    cudaError_t e = cudaStreamSynchronize(t->stream);
+    if (e == cudaSuccess) e = cudaMemcpy(raw.data(), t->ktr, raw.size() * sizeof(uint64_t), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "transformer_trace_read");
+    for (int i = 0; i < n; ++i) {
+        if (kinds) kinds[i] = t->ktr_kind[i];
+        if (!stamps) continue;
+        // reduce the per-slot stamps: earliest start and wait, latest end
+        // (ends are stored complemented, so the latest end is the smallest)
+        const uint64_t* k = raw.data() + (size_t)3 * kKtSlots * i;
+        uint64_t s0 = ~0ull, s1 = ~0ull, s2 = ~0ull;
+        for (int j = 0; j < kKtSlots; ++j) {
+            s0 = k[j] < s0 ? k[j] : s0;
+            s1 = k[kKtSlots + j] < s1 ? k[kKtSlots + j] : s1;
+            s2 = k[2 * kKtSlots + j] < s2 ? k[2 * kKtSlots + j] : s2;
+        }
+        stamps[3 * i] = s0;
+        stamps[3 * i + 1] = s1;
+        stamps[3 * i + 2] = s2 == ~0ull ? ~0ull : ~s2;
+    }
+    return LQ_OK;
 }
 
 int transformer_config(const Transformer* t, Config* cfg, int* kind, int* group_size) {

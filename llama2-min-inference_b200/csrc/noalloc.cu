@@ -93,7 +93,8 @@ extern "C" int matmul_f32_noalloc(float* xout, const float* x, const QuantizedTe
     // device memory is zero-initialised) and goes back to zero whenever
     // lq_sync reports it, so a device-side error of any call stays recorded
     // until the next lq_sync.
-    return lq::matmul_f32_device(xout, x, w, n, d, xq, xs, xsum, err, st, false, num_sms, nullptr);
+    return lq::matmul_f32_device(xout, x, w, n, d, xq, xs, xsum, err, st, lq::launch_flags() & LQ_LAUNCH_PDL, num_sms,
+                                 lq::trace_buffer());
 }
 
 namespace lq {

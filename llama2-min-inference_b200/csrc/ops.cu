@@ -61,6 +61,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     extern __shared__ __align__(16) float asmem[];
     __shared__ __align__(8) uint64_t kv_bar;
     pdl_trigger();
+    kt_start(a.kt);
     const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
     const int hs = a.head_size, km = a.kv_mul;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -94,6 +95,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         bulk_g2s(vs, a.vcache + cbase, bytes, &kv_bar, pol);
     }
     pdl_wait();
+    kt_waited(a.kt);
     const float* qg = a.q + (size_t)b * a.q_stride + (size_t)kvh * km * hs;
     for (int i = tid; i < km * hs; i += kAttnThreads) qs[i] = qg[i];
     __syncthreads();  // also orders the barrier's initialisation before the waits below
@@ -175,7 +177,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
             }
         }
     }
-    if (nsplit == 1) return;
+    if (nsplit == 1) {
+        kt_end_cta(a.kt);
+        return;
+    }
     // last-arriving CTA of this kv head merges the partials
     __threadfence();
     __syncthreads();
@@ -186,7 +191,10 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         if (is_last) *cnt = 0;  // re-arm for the next step
     }
     __syncthreads();
-    if (!is_last) return;
+    if (!is_last) {
+        kt_end_cta(a.kt);
+        return;
+    }
     __threadfence();
     for (int i = tid; i < km * hs; i += kAttnThreads) {
         const int j = i / hs, d = i - j * hs;
@@ -204,6 +212,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         }
         out[i] = o / L;
     }
+    kt_end_cta(a.kt);
 }
 
 size_t attention_smem_bytes(int head_size, int kv_mul) {
@@ -237,9 +246,11 @@ cudaError_t attention_launch(const AttnArgs& a, int batch, cudaStream_t st, bool
 // greedy argmax, sample_argmax runq.c:578-585: first index of the maximum.
 
 __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ logits, int n, int stride,
-                                                      int* __restrict__ out) {
+                                                      int* __restrict__ out, uint64_t* kt) {
     pdl_trigger();
+    kt_start(kt);
     pdl_wait();
+    kt_waited(kt);
     const float* v = logits + (size_t)blockIdx.x * stride;
     float bv = -FLT_MAX;
     int bi = -1;
@@ -279,10 +290,11 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
         }
         if (threadIdx.x == 0) out[blockIdx.x] = bi < 0 ? 0 : bi;
     }
+    kt_end_cta(kt);
 }
 
 cudaError_t argmax_launch(const float* logits, int n, int batch, int stride, int* out, cudaStream_t st,
-                          bool pdl) {
+                          bool pdl, uint64_t* kt) {
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -292,7 +304,7 @@ cudaError_t argmax_launch(const float* logits, int n, int batch, int stride, int
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, argmax_kernel, logits, n, stride, out);
+    return cudaLaunchKernelEx(&cfg, argmax_kernel, logits, n, stride, out, kt);
 }
 
 // ---------------------------------------------------------------------------

@@ -308,7 +308,9 @@ __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_const
     tc_fence_after();
     const uint32_t tmem = bars->tmem_base;
     pdl_trigger();
+    kt_start(a.ep.kt);
     pdl_wait();
+    kt_waited(a.ep.kt);
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -621,6 +623,7 @@ __global__ void __launch_bounds__(kQgThreads, 1) qgemm_kernel(const __grid_const
 
     tc_fence_before();
     __syncthreads();
+    kt_end_cta(a.ep.kt);
     if (warp == kMmaWarp0) {
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols) : "memory");

@@ -225,6 +225,14 @@ static int sample_logits(Sampler* s, float* logits) {
     return s->cand[last].i;
 }
 
+/* first index of the maximum (sample_argmax, runq.c:578-585) */
+static int argmax_first(const float* x, int n) {
+    int best = 0;
+    for (int i = 1; i < n; ++i)
+        if (x[i] > x[best]) best = i;
+    return best;
+}
+
 /* next token after a forward step at (token, pos) */
 static int step(Transformer* t, Sampler* s, int token, int pos, int sample) {
     if (!sample) {
@@ -258,7 +266,29 @@ static void generate(Transformer* t, Vocab* v, Sampler* s, const char* prompt, i
     vocab_encode(v, prompt, 1, 0, toks, &np);
     if (np < 1) die("something is wrong, expected at least 1 prompt token", NULL);
     long start = 0;
-    int token = toks[0], pos = 0;
+    int token = toks[0], pos = 0, timed0 = 1; /* steps timed: those after the first forward call */
+    if (np >= 2 && steps >= np) {
+        /* the whole prompt in one prefill call (rows of one sequence through
+         * every product together), then sample from its last token's logits:
+         * the same tokens and printed pieces as feeding it one at a time */
+        float* logits = forward_prompt(t, toks, np, 0);
+        if (!logits) die("forward failed: ", lq_last_error());
+        for (int i = 0; i + 1 < np; ++i) print_piece(vocab_decode(v, toks[i], toks[i + 1]));
+        fflush(stdout);
+        const int next = s->temperature == 0.0f ? argmax_first(logits, v->n) : sample_logits(s, logits);
+        token = toks[np - 1];
+        pos = np;
+        start = now_ms();
+        timed0 = np;
+        if (next == 1) {
+            printf("\n");
+            free(toks);
+            return;
+        }
+        print_piece(vocab_decode(v, token, next));
+        fflush(stdout);
+        token = next;
+    }
     while (pos < steps) {
         int in_prompt = pos < np - 1;
         int next = step(t, s, token, pos, !in_prompt);
@@ -271,7 +301,7 @@ static void generate(Transformer* t, Vocab* v, Sampler* s, const char* prompt, i
         if (start == 0) start = now_ms();
     }
     printf("\n");
-    if (pos > 1) fprintf(stderr, "achieved tok/s: %f\n", (pos - 1) / (double)(now_ms() - start) * 1000);
+    if (pos > timed0) fprintf(stderr, "achieved tok/s: %f\n", (pos - timed0) / (double)(now_ms() - start) * 1000);
     free(toks);
 }
 

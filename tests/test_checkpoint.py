@@ -98,3 +98,18 @@ def test_tokenizer_format(tmp_path):
         off += 8 + ln
         n += 1
     assert n == 300 and maxlen >= 6
+
+
+@pytest.mark.parametrize("kind,gs", [(8, 32), (4, 32), (8, 64), (4, 128)])
+def test_direct_random_writer_equals_fp32_then_quantize(lq, tmp_path, kind, gs):
+    """lq_write_checkpoint_random writes the bytes of the fp32 export followed
+    by the quantizer (the reference's tools/quantize_int8.py / quantize_int4.py
+    pipeline), without the fp32 intermediate."""
+    import synth
+
+    cfg = lq.Config.make(*synth.SMALL64_CONFIG)
+    f32, a, b = (str(tmp_path / n) for n in ("f.bin", "a.bin", "b.bin"))
+    lq.write_checkpoint_fp32(f32, cfg, 11, 0.02, False)
+    lq.quantize_checkpoint(f32, a, kind, gs)
+    lq.write_checkpoint_random(b, cfg, kind, gs, 11, 0.02)
+    assert open(a, "rb").read() == open(b, "rb").read()

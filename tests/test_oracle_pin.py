@@ -75,9 +75,10 @@ def test_quantizers_are_group_size_parametric(gs):
 def test_oracle_forward_tracks_runq(golden):
     """The oracle's full decode step on the config-1 checkpoint follows
     runq.c.  Teacher-forced with runq's own greedy tokens, the logits agree
-    to 1e-5 relative over the first 64 positions; later positions can differ
-    by an int8 activation rounding flip (a value within an ulp of a rounding
-    boundary), the effect documented in DESIGN.md."""
+    to 1e-5 relative at the golden positions of the first 64; later
+    positions can differ by an int8 activation rounding flip (an fp32 value
+    within an ulp of a rounding boundary, which a different summation order
+    rounds the other way)."""
     import synth
 
     g = golden("tiny_runq.npz")

@@ -77,3 +77,37 @@ def test_runner_starts_like_runq(cuda):
         pytest.skip("runq.c does not run on this host: " + ref.stderr.decode(errors="replace")[:200])
     assert ours.returncode == 0
     assert ours.stdout == ref.stdout
+
+
+RUNQ_CASES = {
+    # chat template with a system prompt (runq.c:731-794), greedy
+    "chat_greedy": ["-m", "chat", "-i", "What is a whale?", "-y", "You answer briefly.", "-t", "0", "-n", "64"],
+    # seeded top-p sampling from BOS (runq.c:604-667: xorshift64*, temperature, nucleus)
+    "sample_t0.8_s7": ["-t", "0.8", "-s", "7", "-n", "64"],
+    # prompt encoding (runq.c:500-560) then seeded sampling
+    "prompt_sample": ["-i", "Once upon a time", "-t", "0.8", "-p", "0.9", "-s", "11", "-n", "64"],
+}
+
+
+@pytest.mark.parametrize("case", sorted(RUNQ_CASES))
+@pytest.mark.parametrize("seed", [42, 1234])
+def test_runner_output_equals_runq(cuda, case, seed):
+    """The runner and runq.c itself, same checkpoint, tokenizer and flags:
+    byte-identical stdout (both computations are deterministic, and their
+    logits agree to ~3e-7 relative until an int8 rounding flip, which these
+    short runs do not turn into a different token)."""
+    if not os.path.exists(RUNQ):
+        pytest.skip("runq.c was not built on this machine")
+    args = [synth.tiny_checkpoint(8, 32, seed=seed), "-z", synth.tiny_tokenizer()] + RUNQ_CASES[case]
+    user_lines = b"Tell me more.\n" * 32  # later chat turns, if the model ends one (token 2)
+    ref = subprocess.run([RUNQ] + args, capture_output=True, timeout=300, input=user_lines,
+                         env=dict(os.environ, OMP_NUM_THREADS="4"))
+    if ref.returncode != 0:
+        pytest.skip("runq.c does not run on this host: " + ref.stderr.decode(errors="replace")[:200])
+    ours = subprocess.run([RUN] + args, capture_output=True, timeout=300, input=user_lines)
+    assert ours.returncode == 0, ours.stderr.decode(errors="replace")
+    n = 0
+    while n < min(len(ours.stdout), len(ref.stdout)) and ours.stdout[n] == ref.stdout[n]:
+        n += 1
+    print(f"{case} seed {seed}: {n} of {len(ref.stdout)} bytes identical")
+    assert ours.stdout == ref.stdout
