@@ -777,8 +777,8 @@ def run_gpu(args):
             "config": {"workload": WORKLOAD, "group_size": GS, "weight_kind": "int8", "batch": 1,
                        "bytes_per_step": sb, "l2": f"{COPIES} weight copies ({COPIES * sb / 1e9:.2f} GB) alternate; "
                        "inputs larger than L2", "parallelism": f"replicas x{world}",
-                       "launch": "CUDA graph per step: 8 GEMV launches (each quantizes its fp32 input in its "
-                                 "prologue), programmatic dependent launch",
+                       "launch": "CUDA graph per step: 8 x (activation quantizer + GEMV), programmatic dependent "
+                                 "launch",
                        "per_shape_us": per_shape},
             "roofline": {"bound": "hbm", "achieved": round(per_gpu_gbs, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(per_gpu_gbs / peak, 4), "peak_source": peak_kind,
@@ -792,7 +792,7 @@ def run_gpu(args):
                     "h2d_bytes_per_step": sum(4 * n for n, d in SHAPES),
                     "d2h_bytes_per_step": sum(4 * d for n, d in SHAPES),
                     "path": "matmul_f32 C ABI, pinned host x and y, copies + sync inside each call"},
-            "gpu_launches": args.steps * len(SHAPES),
+            "gpu_launches": args.steps * 2 * len(SHAPES),
             "clocks": clk,
         }
         line.update(extra)

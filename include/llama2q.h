@@ -133,11 +133,11 @@ int quantize(QuantizedTensor* out, const float* x, int n);
  * with the same group size; xout: fp32 [B, d].  All device memory. */
 int matmul(float* xout, const QuantizedTensor* x, const QuantizedTensor* w, int n, int d);
 
-/* fp32-input form: quantize x (group size of w) inside the GEMV prologue and
- * multiply, i.e. runq.c's quantize_act followed by matmul_q8 (runq.c:345-348)
- * in one launch.  x fp32 [n] and xout fp32 [d] may be host or device
- * memory; with host memory the copies are part of the call, which then
- * returns after the result is in xout. */
+/* fp32-input form: quantize x with the group size of w, then multiply, i.e.
+ * runq.c's quantize_act followed by matmul_q8 (runq.c:345-348): two kernels,
+ * the GEMV streaming its first weights while the quantizer runs.  x fp32 [n]
+ * and xout fp32 [d] may be host or device memory; with host memory the copies
+ * are part of the call, which then returns after the result is in xout. */
 int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int d);
 
 /* Allocation-free form of matmul_f32, for callers that cannot allocate device

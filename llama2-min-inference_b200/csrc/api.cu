@@ -387,23 +387,14 @@ int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int
     const bool xdev = is_device_ptr(x), ydev = is_device_ptr(xout);
     if ((reinterpret_cast<uintptr_t>(x) & 15u) && xdev)
         return lq_fail(LQ_EINVAL, "matmul_f32: device x must be 16-byte aligned");
-    static int fused = -1;
-    if (fused < 0) {
-        const char* e = getenv("LQ_MATMUL_FUSED");
-        fused = e ? atoi(e) : 0;
-    }
     const int ng = n / w->group_size;
     auto up = [](size_t v) { return (v + 255) / 256 * 256; };
-    // scratch: [fp32 x (host input)] [fp32 y (host output)] and, for the
-    // two-launch form, [int8 xq] [fp32 xs] [int32 xsum]
+    // scratch: [fp32 x (host input only)] [fp32 y (host output only)] [int8 xq] [fp32 xs] [int32 xsum]
     const size_t off_y = xdev ? 0 : up((size_t)n * 4);
     const size_t off_xq = off_y + (ydev ? 0 : up((size_t)d * 4));
     const size_t off_xs = off_xq + up((size_t)n), off_xsum = off_xs + up((size_t)ng * 4);
-    const size_t need = fused ? off_xq : off_xsum + up((size_t)ng * 4);
-    if (need) {
-        rc = ensure_scratch(c, need);
-        if (rc) return rc;
-    }
+    rc = ensure_scratch(c, off_xsum + up((size_t)ng * 4));
+    if (rc) return rc;
     char* sc = static_cast<char*>(c->scratch);
     const float* xd = x;
     float* yd = ydev ? xout : reinterpret_cast<float*>(sc + off_y);
@@ -412,29 +403,13 @@ int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int
         if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of x");
         xd = reinterpret_cast<const float*>(sc);
     }
-    if (fused) {
-        // one launch: every CTA quantizes x in its prologue (quantize_act's
-        // arithmetic, runq.c:117-139) while its first weight copies are in flight
-        GemvArgs a = {};
-        a.seg[0] = {static_cast<const uint8_t*>(w->q), w->s, yd, d, EPI_STORE};
-        a.nseg = 1;
-        a.cols = n;
-        a.gs = w->group_size;
-        a.nb = 1;
-        a.in_mode = IN_F32;
-        a.xf = xd;
-        a.y_stride = d;
-        a.err = c->err;
-        a.trace = g_trace;
-        cudaError_t e = gemv_launch(a, w->kind, g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms);
-        if (e != cudaSuccess) return cuda_fail(e, "matmul_f32 launch");
-    } else {
-        // the activation quantizer, then the GEMV from the int8 activation
-        rc = lq::matmul_f32_device(yd, xd, w, n, d, reinterpret_cast<int8_t*>(sc + off_xq),
-                                   reinterpret_cast<float*>(sc + off_xs), reinterpret_cast<int*>(sc + off_xsum), c->err,
-                                   g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms, g_trace);
-        if (rc) return rc;
-    }
+    // the activation quantizer (quantize_act, runq.c:117-139), then the GEMV
+    // from the int8 activation; the GEMV streams its first weights while the
+    // quantizer runs
+    rc = lq::matmul_f32_device(yd, xd, w, n, d, reinterpret_cast<int8_t*>(sc + off_xq),
+                               reinterpret_cast<float*>(sc + off_xs), reinterpret_cast<int*>(sc + off_xsum), c->err,
+                               g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms, g_trace);
+    if (rc) return rc;
     if (!xdev || !ydev) {
         cudaError_t e = cudaSuccess;
         if (!ydev) e = cudaMemcpyAsync(xout, yd, (size_t)d * 4, cudaMemcpyDeviceToHost, g_stream);

@@ -299,35 +299,6 @@ __device__ void stage_input(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum
     }
 }
 
-// Cluster exchange: copy the other CTAs' slices of the staged activation
-// (int8 values, group scales and sums) from their shared memory into this
-// CTA's, at the same offsets.  Each slice is groups [p*ng/cs, (p+1)*ng/cs) of
-// every row; INT4 rows are two planes of n/2 bytes (even / odd values).
-template <int KIND>
-__device__ void gather_slices(const GemvArgs& a, int8_t* xsm, float* xs, int* xsum, int ctid, int nt, int rank,
-                              int cs) {
-    const int n = a.cols, gs = a.gs, ng = n / gs;
-    for (int p = 0; p < cs; ++p) {
-        if (p == rank) continue;
-        const int pg0 = p * ng / cs, pg1 = (p + 1) * ng / cs, sg = pg1 - pg0;
-        const int half = KIND == 8 ? sg * gs / 16 : sg * gs / 32;  // 16-byte units per plane
-        const int upr = KIND == 8 ? half : 2 * half;
-        const uint32_t rx = cluster_map(xsm, p);
-        for (int i = ctid; i < a.nb * upr; i += nt) {
-            const int b = i / upr, k = i - b * upr;
-            const int off = KIND == 8 ? b * n + pg0 * gs + 16 * k
-                                      : b * n + (k < half ? 0 : n / 2) + pg0 * gs / 2 + 16 * (k < half ? k : k - half);
-            *reinterpret_cast<uint4*>(xsm + off) = ld_cluster_v4(rx + off);
-        }
-        const uint32_t rs = cluster_map(xs, p), rq = cluster_map(xsum, p);
-        for (int i = ctid; i < a.nb * sg; i += nt) {
-            const int g = (i / sg) * ng + pg0 + i % sg;
-            xs[g] = __uint_as_float(ld_cluster_u32(rs + 4 * g));
-            xsum[g] = (int)ld_cluster_u32(rq + 4 * g);
-        }
-    }
-}
-
 // ---------------------------------------------------------------------------
 // dot products
 
@@ -427,12 +398,7 @@ __device__ __forceinline__ void block_dot(const uint8_t* const* rows, const floa
     }
 }
 
-// epilogue (rope_pair, finish_rows): lq_epilogue.cuh.  Called out of line
-// (by one lane per row pair), so the kernels hold one copy of its cases.
-__device__ __noinline__ void finish_rows_call(const GemvArgs& a, const GemvSeg& g, int b, int r, float v0, float v1,
-                                              float u0, float u1, bool has2) {
-    finish_rows(a, g, b, r, v0, v1, u0, u1, has2);
-}
+// epilogue (rope_pair, finish_rows): lq_epilogue.cuh
 
 // ---------------------------------------------------------------------------
 // the kernel
@@ -572,8 +538,8 @@ __global__ void __launch_bounds__(kGemvThreads, NB == 1 ? 4 : (NB == 2 ? 2 : 1))
         if (lane == 0) {
 #pragma unroll
             for (int b = 0; b < NB; ++b) {
-                finish_rows_call(a, g, b, r, v[0][b], v[1][b], u[0][b], u[1][b], has2);
-                if (second) finish_rows_call(a, g, b, r + 2, v[2 % NR][b], v[3 % NR][b], 0.0f, 0.0f, true);
+                finish_rows(a, g, b, r, v[0][b], v[1][b], u[0][b], u[1][b], has2);
+                if (second) finish_rows(a, g, b, r + 2, v[2 % NR][b], v[3 % NR][b], 0.0f, 0.0f, true);
             }
         }
         p += npairs;
@@ -640,7 +606,7 @@ __device__ __forceinline__ bool titem_next(const GemvArgs& a, TIter& it, int rb,
     return true;
 }
 
-__device__ __noinline__ void titem_issue(const GemvArgs& a, const TItem& it, uint8_t* slot, uint64_t* bar, int rb,
+__device__ __forceinline__ void titem_issue(const GemvArgs& a, const TItem& it, uint8_t* slot, uint64_t* bar, int rb,
                                             int ng, int gb, int tw, uint64_t pol) {
     const GemvSeg& g = a.seg[it.seg];
     const int mult = a.paired ? 2 : 1;
@@ -817,17 +783,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
     pdl_wait();
     kt_waited(a.kt);
     if (tr && threadIdx.x == 0) tr[1] = globaltimer();
-    // In a cluster each CTA builds one slice of the activation and reads the
-    // others from its peers' shared memory (the activation is read from L2 by
-    // every cluster once, not by every CTA).
-    const int cs = (int)cluster_size(), crank = (int)cluster_rank();
-    stage_input<KIND>(a, xsm, xs, xsum, red, threadIdx.x, blockDim.x, crank * ng / cs, (crank + 1) * ng / cs);
-    if (cs > 1) {
-        cluster_arrive();  // this CTA's slice is written ...
-        cluster_wait();    // ... and so is every peer's
-        gather_slices<KIND>(a, xsm, xs, xsum, threadIdx.x, blockDim.x, crank, cs);
-        cluster_arrive();  // done reading the peers (each waits for this before it exits)
-    }
+    stage_input<KIND>(a, xsm, xs, xsum, red, threadIdx.x, blockDim.x, 0, ng);
     __syncthreads();
     if (tr && threadIdx.x == 0) tr[2] = globaltimer();
     // every lane walks the issue iterator too (lane 0 already advanced it)
@@ -840,9 +796,10 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
     for (int b = 0; b < NB; ++b) acc[0][b] = acc[1][b] = acc2[0][b] = acc2[1][b] = 0.0f;
     for (int k = 0; titem_next(a, cmp, rb, it); ++k) {
         const int s = k & 1;
+        // the decision to give up is warp-uniform: the lanes then leave the
+        // loop together (no lane is left inside a warp-wide shuffle)
         if (!__all_sync(0xffffffffu, mbar_wait(&bar[s], (k >> 1) & 1, a.err, DEV_TIMEOUT_FULL))) {
-            // give up: confirm the copy of the other slot too, then leave the
-            // loop (the CTA still takes its part in the cluster's last barrier)
+            // give up: confirm the copy of the other slot too, then leave
             if (lane == 0) mbar_wait(&bar[s ^ 1], ((k + 1) >> 1) & 1, a.err, DEV_TIMEOUT_DRAIN);
             break;
         }
@@ -873,9 +830,8 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
 #pragma unroll
                     for (int b = 0; b < NB; ++b) v[q][b] = warp_sum(v[q][b]);
                 if (lane == 0) {
-#pragma unroll 1
-                    for (int b = 0; b < NB; ++b)
-                        finish_rows_call(a, g, b, it.row + r, v[0][b], v[1][b], v[2][b], v[3][b], true);
+#pragma unroll
+                    for (int b = 0; b < NB; ++b) finish_rows(a, g, b, it.row + r, v[0][b], v[1][b], v[2][b], v[3][b], true);
                 }
             }
         } else {
@@ -912,7 +868,7 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
                     const float v0 = warp_sum(acc[0][b]), v1 = warp_sum(acc[1][b]);
                     const float u0 = PAIRED ? warp_sum(acc2[0][b]) : 0.0f, u1 = PAIRED ? warp_sum(acc2[1][b]) : 0.0f;
                     acc[0][b] = acc[1][b] = acc2[0][b] = acc2[1][b] = 0.0f;
-                    if (lane == 0) finish_rows_call(a, g, b, it.row, v0, v1, u0, u1, true);
+                    if (lane == 0) finish_rows(a, g, b, it.row, v0, v1, u0, u1, true);
                 }
             }
         }
@@ -926,7 +882,6 @@ __global__ void __launch_bounds__(kTmaMaxWarps * 32, 1) gemv_tma_kernel(const __
         }
     }
     kt_end_cta(a.kt);
-    if (cs > 1) cluster_wait();  // no peer reads this CTA's shared memory any more
     if (tr) {
         __syncthreads();
         if (threadIdx.x == 0) tr[3] = globaltimer();
@@ -1244,47 +1199,6 @@ static int g_use_tma = -1;
 // Shared-memory budget per bulk-copy GEMV CTA: two CTAs (of consecutive
 // kernels) fit one SM's 228 KB with 1 KB reserved each.  LQ_GEMV_SMEM_KB
 // overrides it (for tuning).
-// Weight items (of two) each warp requests before the wait for the previous
-// kernel, and the most warps per CTA (tuning: LQ_GEMV_PREFETCH, LQ_GEMV_MAXWARPS).
-static int gemv_prefetch_items() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("LQ_GEMV_PREFETCH");
-        v = e ? atoi(e) : 2;
-        if (v < 0 || v > 2) v = 2;
-    }
-    return v;
-}
-// CTAs per cluster sharing the activation staging (1, 2 or 4; LQ_GEMV_CLUSTER)
-static int gemv_cluster() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("LQ_GEMV_CLUSTER");
-        v = e ? atoi(e) : 1;
-        if (v != 1 && v != 2 && v != 4) v = 1;
-    }
-    return v;
-}
-static int gemv_max_warps() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("LQ_GEMV_MAXWARPS");
-        v = e ? atoi(e) : kTmaMaxWarps;
-        if (v < 4 || v > kTmaMaxWarps) v = kTmaMaxWarps;
-    }
-    return v;
-}
-
-static int gemv_smem_target() {
-    static int v = -1;
-    if (v < 0) {
-        const char* e = getenv("LQ_GEMV_SMEM_KB");
-        v = (e ? atoi(e) : 227) * 1024;
-        if (v < 32 * 1024 || v > 227 * 1024) v = 227 * 1024;
-    }
-    return v;
-}
-
 template <int KIND, int NB, int CPG>
 static cudaError_t launch_tma(GemvArgs a, cudaStream_t st, bool pdl, int num_sms) {
     const int rb = KIND == 8 ? a.cols : a.cols / 2;
@@ -1308,17 +1222,9 @@ static cudaError_t launch_tma(GemvArgs a, cudaStream_t st, bool pdl, int num_sms
     int P = 0;
     for (int i = 0; i < a.nseg; ++i) P += a.seg[i].rows / 2;
     if (P == 0) return cudaSuccess;
-    // Warps (two slots each): as many as fit half an SM's shared memory, so
-    // that the next kernel's CTA can be resident beside this one and stream
-    // its first weights while this one finishes; at least four warps, else as
-    // many as fit the whole SM (up to 16).
+    // as many warps (two slots each) as shared memory holds, up to 16
     int nw = 0;
-    const int wmax = gemv_max_warps();
-    for (int w = wmax; w >= 4 && !nw; --w) {
-        a.nstages = 2 * w;
-        if (make_layout(a).total <= gemv_smem_target()) nw = w;
-    }
-    for (int w = wmax; w >= 4 && !nw; --w) {
+    for (int w = kTmaMaxWarps; w >= 4 && !nw; w -= 2) {
         a.nstages = 2 * w;
         if (make_layout(a).total <= 227 * 1024) nw = w;
     }
@@ -1338,40 +1244,16 @@ static cudaError_t launch_tma(GemvArgs a, cudaStream_t st, bool pdl, int num_sms
     cudaLaunchConfig_t cfg = {};
     int grid = (P + nw - 1) / nw;
     if (grid > num_sms) grid = num_sms;
-    // clusters of cs CTAs share the activation staging (grid a multiple of cs,
-    // and no larger than the clusters that can be resident at once)
-    int cs = gemv_cluster();
-    if (cs > 1 && (grid < cs || ng < cs)) cs = 1;
-    if (cs > 1) grid = grid / cs * cs;
-    cudaLaunchAttribute attr[2];
-    int na = 0;
-    if (pdl) {
-        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        attr[na].val.programmaticStreamSerializationAllowed = 1;
-        ++na;
-    }
-    if (cs > 1) {
-        attr[na].id = cudaLaunchAttributeClusterDimension;
-        attr[na].val.clusterDim.x = cs;
-        attr[na].val.clusterDim.y = 1;
-        attr[na].val.clusterDim.z = 1;
-        ++na;
-    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(nw * 32);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = st;
     cfg.attrs = attr;
-    cfg.numAttrs = na;
-    if (cs > 1) {
-        int mc = 0;
-        if (cudaOccupancyMaxActiveClusters(&mc, kern, &cfg) == cudaSuccess && mc >= 1 && mc * cs < grid) {
-            grid = mc * cs;
-            cfg.gridDim = dim3(grid);
-        }
-        cudaGetLastError();
-    }
-    return cudaLaunchKernelEx(&cfg, kern, a, pdl ? gemv_prefetch_items() : 0);
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, a, pdl ? 2 : 0);
 }
 
 template <int KIND, int NB, int CPG>

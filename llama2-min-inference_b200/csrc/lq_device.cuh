@@ -144,41 +144,6 @@ __device__ __forceinline__ void set_err(int* err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
-// Thread-block clusters (distributed shared memory), public PTX ISA.
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ uint32_t cluster_size() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
-    return r;
-}
-__device__ __forceinline__ void cluster_arrive() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
-// the address of this CTA's shared-memory location `p` in CTA `rank` of the cluster
-__device__ __forceinline__ uint32_t cluster_map(const void* p, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(p)), "r"(rank));
-    return r;
-}
-__device__ __forceinline__ uint4 ld_cluster_v4(uint32_t addr) {
-    uint4 v;
-    asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "r"(addr)
-                 : "memory");
-    return v;
-}
-__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
-    uint32_t v;
-    asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
-    return v;
-}
-
 // Step trace (profiling; kt == nullptr: off).  kt holds this kernel's
 // stamps (globaltimer ns) in 3 x kKtSlots words, each reduced over the CTAs
 // that share a slot (blockIdx.x % kKtSlots) with atomicMin from an all-ones

@@ -344,105 +344,6 @@ uint64_t* kt_next(Transformer* t, int kind) {
     return t->ktr + 3 * kKtSlots * (size_t)t->ktr_n++;
 }
 
-// The decode step for 1..mma_min-1 sequences on one GPU: five kernels per
-// layer.  Every GEMV builds its int8 activation in its own prologue (rmsnorm
-// + quantize_act, or quantize_act of the fp32 input, with the stand-alone
-// quantizer's arithmetic), so no quantizer kernel sits between the products:
-//   GEMV [wq|wk|wv]  prologue rmsnorm(x) (layer 0: x = emb[token])  epilogue RoPE / K, V cache
-//   attention
-//   GEMV wo          prologue quantize(att)                          epilogue x += .
-//   GEMV [w1|w3]     prologue rmsnorm(x)                             epilogue SwiGLU
-//   GEMV w2          prologue quantize(h)                            epilogue x += .
-// then the classifier GEMV (prologue: final rmsnorm) and argmax.
-template <typename Base>
-static int forward_fused(Transformer* t, int batch, Base& base) {
-    const Config& c = t->c;
-    const int kind = t->kind;
-    const int D = c.dim, DQ = t->dq_l, H = t->hid_l, KV = t->kv_dim, hs = t->head_size, gs = t->gs;
-    const int64_t rbD = rbytes(D, kind), rbQ = rbytes(DQ, kind), rbH = rbytes(H, kind);
-    const int ngD = D / gs, ngQ = DQ / gs, ngH = H / gs;
-    const int64_t kv_layer = (int64_t)t->nkv_l * t->max_seq * hs;
-    // decode: row b is sequence b (its own cache); prompt: every row is a
-    // position of sequence prompt_seq (one cache, no stride between rows)
-    const int64_t kv_seq = t->prompt_seq >= 0 ? 0 : (int64_t)c.n_layers * kv_layer;
-    float* const kc = t->kc + (t->prompt_seq >= 0 ? (int64_t)t->prompt_seq * c.n_layers * kv_layer : 0);
-    float* const vc = t->vc + (t->prompt_seq >= 0 ? (int64_t)t->prompt_seq * c.n_layers * kv_layer : 0);
-    cudaStream_t st = t->stream;
-    cudaError_t e;
-    float* x = t->x;
-    for (int l = 0; l < c.n_layers; ++l) {
-        GemvArgs a;
-        base(a, D);
-        a.seg[0] = {t->wq.q + (size_t)l * DQ * rbD, t->wq.s + (size_t)l * DQ * ngD, t->q, DQ, EPI_ROPE_Q};
-        a.seg[1] = {t->wk.q + (size_t)l * KV * rbD, t->wk.s + (size_t)l * KV * ngD, nullptr, KV, EPI_ROPE_KCACHE};
-        a.seg[2] = {t->wv.q + (size_t)l * KV * rbD, t->wv.s + (size_t)l * KV * ngD, nullptr, KV, EPI_VCACHE};
-        a.nseg = 3;
-        a.y_stride = DQ;
-        a.in_mode = l == 0 ? IN_RMSNORM_EMB : IN_RMSNORM;
-        a.xf = x;
-        a.rms_w = t->rms_att + (size_t)l * D;
-        a.emb = t->emb;
-        a.x_out = x;
-        a.kcache = kc + l * kv_layer;
-        a.vcache = vc + l * kv_layer;
-        if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
-        AttnArgs at{};
-        at.q = t->q;
-        at.kcache = kc + l * kv_layer;
-        at.vcache = vc + l * kv_layer;
-        at.out = t->att;
-        at.part = t->part;
-        at.counters = t->counters;
-        at.meta = t->meta;
-        at.err = t->err;
-        at.kv_seq_stride = kv_seq;
-        at.q_stride = DQ;
-        at.n_heads = t->nh_l;
-        at.n_kv_heads = t->nkv_l;
-        at.kv_mul = t->kv_mul;
-        at.head_size = hs;
-        at.max_seq = t->max_seq;
-        at.max_splits = t->max_splits;
-        at.kt = kt_next(t, LQ_TRACE_ATTENTION);
-        if ((e = attention_launch(at, batch, st, true)) != cudaSuccess) return cuda_fail(e, "attention");
-        base(a, DQ);
-        a.seg[0] = {t->wo.q + (size_t)l * D * rbQ, t->wo.s + (size_t)l * D * ngQ, x, D, EPI_ADD};
-        a.nseg = 1;
-        a.in_mode = IN_F32;
-        a.xf = t->att;
-        if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "wo gemv");
-        base(a, D);
-        a.seg[0] = {t->w1.q + (size_t)l * H * rbD, t->w1.s + (size_t)l * H * ngD, t->h1, H, EPI_SWIGLU,
-                    t->w3.q + (size_t)l * H * rbD, t->w3.s + (size_t)l * H * ngD};
-        a.nseg = 1;
-        a.paired = 1;
-        a.y_stride = H;
-        a.in_mode = IN_RMSNORM;
-        a.xf = x;
-        a.rms_w = t->rms_ffn + (size_t)l * D;
-        if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "w1/w3 gemv");
-        base(a, H);
-        a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, x, D, EPI_ADD};
-        a.nseg = 1;
-        a.in_mode = IN_F32;
-        a.xf = t->h1;
-        if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
-    }
-    GemvArgs a;
-    base(a, D);
-    a.seg[0] = {t->wcls.q, t->wcls.s, t->logits, c.vocab_size, EPI_STORE};
-    a.nseg = 1;
-    a.y_stride = c.vocab_size;
-    a.in_mode = IN_RMSNORM;
-    a.xf = x;
-    a.rms_w = t->rms_final;
-    if ((e = gemv_rows(t, a, kind, batch, st)) != cudaSuccess) return cuda_fail(e, "classifier gemv");
-    if ((e = argmax_launch(t->logits, c.vocab_size, batch, c.vocab_size, t->next, st, true,
-                           kt_next(t, LQ_TRACE_ARGMAX))) != cudaSuccess)
-        return cuda_fail(e, "argmax");
-    return LQ_OK;
-}
-
 // Issue one decode step for `batch` sequences on t->stream (capturable).
 int forward_launch(Transformer* t, int batch) {
     t->ktr_n = 0;
@@ -561,12 +462,6 @@ int forward_launch(Transformer* t, int batch) {
     float* xa = t->x;              // residual stream after attention's add (and the embedding)
     float* xb = t->tp ? t->x2 : t->x;  // after the ffn's add
     int rc;
-    static int fused = -1;
-    if (fused < 0) {
-        const char* e = getenv("LQ_DECODE_FUSED");
-        fused = e ? atoi(e) : 0;
-    }
-    if (fused && !t->tp && !use_mma(t, batch)) return forward_fused(t, batch, base);
     for (int l = 0; l < c.n_layers; ++l) {
         GemvArgs a;
         // 1. q, k, v (attention rmsnorm + quantize first; layer 0 starts from emb[token])
@@ -661,11 +556,8 @@ int kernels_per_step(const Transformer* t, int batch) {
     }
     const int cd = gemv_chunk(t->c.dim), ch = gemv_chunk(t->hid_l), cq = gemv_chunk(t->dq_l);
     const int gd = (batch + cd - 1) / cd, gh = (batch + ch - 1) / ch, gq = (batch + cq - 1) / cq;
-    if (t->tp || !getenv("LQ_DECODE_FUSED") || atoi(getenv("LQ_DECODE_FUSED")) == 0)
-        // per layer: 4 quantizers, attention, GEMVs qkv / wo / w1|w3 / w2
-        return t->c.n_layers * (5 + 2 * gd + gq + gh) + 2 + gd;
-    // per layer: attention and the GEMVs qkv / wo / w1|w3 / w2, each quantizing its own input
-    return t->c.n_layers * (1 + 2 * gd + gq + gh) + 1 + gd;
+    // per layer: 4 quantizers, attention, GEMVs qkv / wo / w1|w3 / w2
+    return t->c.n_layers * (5 + 2 * gd + gq + gh) + 2 + gd;
 }
 
 static int ensure_graph(Transformer* t, int batch) {

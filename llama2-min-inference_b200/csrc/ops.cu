@@ -196,21 +196,43 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         return;
     }
     __threadfence();
-    for (int i = tid; i < km * hs; i += kAttnThreads) {
-        const int j = i / hs, d = i - j * hs;
-        const float* base = a.part + (((size_t)b * a.n_heads + hq0 + j) * a.max_splits) * (hs + 2);
-        float M = -FLT_MAX;
-#pragma unroll 8
-        for (int s = 0; s < nsplit; ++s) M = fmaxf(M, __ldcg(base + (size_t)s * (hs + 2)));
-        float L = 0.0f, o = 0.0f;
-#pragma unroll 4
-        for (int s = 0; s < nsplit; ++s) {
-            const float* ps = base + (size_t)s * (hs + 2);
-            const float w = lq_expf(__ldcg(ps) - M);
-            L = fmaf(__ldcg(ps + 1), w, L);
-            o = fmaf(__ldcg(ps + 2 + d), w, o);
+    // The partials of a group of heads are first copied into shared memory
+    // (the K / V chunk buffers are free by now) by every thread at once, so
+    // the merge waits for one round of L2 loads, not one per chunk; the merge
+    // arithmetic itself is unchanged: M = max over the chunks, then L and o
+    // accumulated with fmaf in chunk order.
+    const int per_head = nsplit * (hs + 2);
+    const int cap = 2 * kChunk * hs;                    // floats of the K and V buffers
+    const int hb = cap / per_head < 1 ? 1 : (cap / per_head < km ? cap / per_head : km);
+    const bool staged = per_head <= cap;
+    for (int j0 = 0; j0 < km; j0 += hb) {
+        const int nh = km - j0 < hb ? km - j0 : hb;
+        if (staged) {
+            __syncthreads();  // the previous group's reads of the buffer are done
+            for (int hh = 0; hh < nh; ++hh) {
+                const float* src = a.part + (((size_t)b * a.n_heads + hq0 + j0 + hh) * a.max_splits) * (hs + 2);
+                float* dst = ks + hh * per_head;
+                for (int i = tid; i < per_head; i += kAttnThreads) dst[i] = __ldcg(src + i);
+            }
+            __syncthreads();
         }
-        out[i] = o / L;
+        for (int i = tid; i < nh * hs; i += kAttnThreads) {
+            const int jj = i / hs, d = i - jj * hs, j = j0 + jj;
+            const float* base = staged ? ks + jj * per_head
+                                       : a.part + (((size_t)b * a.n_heads + hq0 + j) * a.max_splits) * (hs + 2);
+            float M = -FLT_MAX;
+#pragma unroll 8
+            for (int s = 0; s < nsplit; ++s) M = fmaxf(M, base[(size_t)s * (hs + 2)]);
+            float L = 0.0f, o = 0.0f;
+#pragma unroll 4
+            for (int s = 0; s < nsplit; ++s) {
+                const float* ps = base + (size_t)s * (hs + 2);
+                const float w = lq_expf(ps[0] - M);
+                L = fmaf(ps[1], w, L);
+                o = fmaf(ps[2 + d], w, o);
+            }
+            out[j * hs + d] = o / L;
+        }
     }
     kt_end_cta(a.kt);
 }

@@ -77,6 +77,13 @@ def ref() -> C.CDLL:
         L.ref_vocab.argtypes = [_P]
         L.ref_free.argtypes = [_P]
         L.ref_set_threads.argtypes = [I]
+        L.ref_tokenizer.restype = _P
+        L.ref_tokenizer.argtypes = [C.c_char_p, I]
+        L.ref_encode.restype = I
+        L.ref_encode.argtypes = [_P, C.c_char_p, _P]
+        L.ref_tokenizer_free.argtypes = [_P]
+        L.ref_sample.restype = I
+        L.ref_sample.argtypes = [_P, I, C.c_float, C.c_float, C.POINTER(C.c_ulonglong)]
         L.ref_act_trace.restype = C.c_long
         L.ref_act_trace.argtypes = [_P, _P, C.c_long]
         _ref = L
@@ -258,6 +265,23 @@ def ref_matmul_q8(xq, xs, xt, q_biased, s, rows: int, cols: int) -> np.ndarray:
                         _ptr(np.ascontiguousarray(xt)), _ptr(np.ascontiguousarray(q_biased)),
                         _ptr(np.ascontiguousarray(s)), rows, cols)
     return out
+
+
+def ref_sample(logits: np.ndarray, temperature: float, topp: float, state: int):
+    """runq.c's sample() on a copy of the logits: (next token, new rng state)."""
+    x = np.ascontiguousarray(logits, np.float32).copy()
+    st = C.c_ulonglong(state)
+    nxt = ref().ref_sample(_ptr(x), x.size, temperature, topp, C.byref(st))
+    return nxt, st.value
+
+
+def ref_encode(tokenizer_path: str, vocab: int, text: str) -> np.ndarray:
+    """runq.c's encode of a prompt (BOS first, no EOS), as generate() calls it."""
+    t = ref().ref_tokenizer(tokenizer_path.encode(), vocab)
+    out = np.zeros(len(text.encode()) + 3, np.int32)
+    n = ref().ref_encode(t, text.encode(), _ptr(out))
+    ref().ref_tokenizer_free(t)
+    return out[:n].copy()
 
 
 def ref_quantize_act(x: np.ndarray):

@@ -90,5 +90,36 @@ void ref_free(void* t) {
 
 int ref_group_size(void) { return QBLOCK; }
 
+/* runq.c's sampler (runq.c:587-667: temperature, softmax, xorshift64* coin,
+ * multinomial or top-p) on the given logits (modified in place); *rng is the
+ * sampler's state, advanced as runq.c advances it. */
+int ref_sample(float* logits, int n, float temperature, float topp, unsigned long long* rng) {
+    Sampler sp;
+    build_sampler(&sp, n, temperature, topp, *rng);
+    int next = sample(&sp, logits);
+    *rng = sp.rng_state;
+    free_sampler(&sp);
+    return next;
+}
+
+/* runq.c's tokenizer (runq.c:444-560): load tokenizer.bin, encode text as
+ * generate() does (BOS, no EOS), release. */
+void* ref_tokenizer(const char* path, int vocab_size) {
+    Tokenizer* t = (Tokenizer*)calloc(1, sizeof(Tokenizer));
+    build_tokenizer(t, (char*)path, vocab_size);
+    return t;
+}
+
+int ref_encode(void* t, const char* text, int* tokens) {
+    int n = 0;
+    encode((Tokenizer*)t, (char*)text, 1, 0, tokens, &n);
+    return n;
+}
+
+void ref_tokenizer_free(void* t) {
+    free_tokenizer((Tokenizer*)t);
+    free(t);
+}
+
 void ref_set_threads(int n) { omp_set_num_threads(n); }
 int ref_max_threads(void) { return omp_get_max_threads(); }

@@ -99,3 +99,67 @@ def matched_prefix(a, b) -> int:
 
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def _pieces(tokenizer_path: str, vocab: int):
+    import struct
+
+    with open(tokenizer_path, "rb") as f:
+        f.read(4)
+        out = []
+        for _ in range(vocab):
+            _, n = struct.unpack("<fi", f.read(8))
+            out.append(f.read(n))
+    return out
+
+
+def runq_piece(pieces, prev: int, tok: int) -> bytes:
+    """runq.c's decode + safe_printf (runq.c:474-498): the bytes printed for
+    token `tok` after `prev`."""
+    p = pieces[tok]
+    if prev == 1 and p[:1] == b" ":
+        p = p[1:]
+    if len(p) == 6 and p.startswith(b"<0x") and p.endswith(b">"):
+        p = bytes([int(p[3:5], 16)])
+    if len(p) == 1 and not (0x20 <= p[0] <= 0x7E or p[0] in (9, 10, 11, 12, 13)):  # C-locale isprint / isspace
+        return b""
+    return p
+
+
+def runq_generate_greedy(path: str, tokenizer_path: str, prompt: str, steps: int):
+    """runq.c's generate() with -t 0, replayed through its own forward and
+    encoder (the build shim): the token fed at every position, and the bytes
+    printed after each position (runq.c:681-716)."""
+    vocab = synth.TINY_CONFIG[5]
+    ids = O.ref_encode(tokenizer_path, vocab, prompt)
+    pieces = _pieces(tokenizer_path, vocab)
+    R = O.RefRunq(path)
+    fed, printed = [], []
+    token = int(ids[0])
+    for pos in range(steps):
+        lg = R.forward(token, pos)
+        nxt = int(ids[pos + 1]) if pos < len(ids) - 1 else int(np.argmax(lg))
+        fed.append(token)
+        if nxt == 1:
+            break
+        printed.append(runq_piece(pieces, token, nxt))
+        token = nxt
+    R.close()
+    return fed, printed
+
+
+def first_flip_along(path: str, fed, config=synth.TINY_CONFIG) -> int:
+    """First position whose int8 activations differ between runq.c and the
+    kernel-order oracle (the device's arithmetic) when both are fed `fed`
+    (len(fed) if none)."""
+    R, M = O.RefRunq(path), O.OracleModel(path)
+    first = len(fed)
+    for pos, tok in enumerate(fed):
+        _, rq, _ = R.forward_traced(int(tok), pos, config)
+        _, oq = M.forward_kernel_order_traced(int(tok), pos)
+        if not np.array_equal(rq, oq):
+            first = pos
+            break
+    R.close()
+    M.close()
+    return first
