@@ -35,6 +35,7 @@
 //  * Every wait is bounded (2 s); on expiry the kernel records an error code,
 //    the producer confirms its in-flight copies (bounded) and all threads
 //    return.
+#include <cfloat>
 #include <cstdio>
 #include <cstdlib>
 
@@ -42,6 +43,7 @@
 #include "lq_epilogue.cuh"
 #include "lq_kernels.h"
 #include "lq_math.h"
+#include "lq_ops.h"
 
 namespace lq {
 
@@ -1031,6 +1033,134 @@ cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl) {
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, act_quant_kernel, a);
+}
+
+// ---------------------------------------------------------------------------
+// attention merge + quantize: a thread per value of the row, a CTA per 256
+// values (whole quantization groups: gs divides 256).
+//
+// Merge (the split-KV merge order, runq.c:369-391 restated for chunks of
+// kChunk positions): M = max over the chunks of m_s; w_s = exp(m_s - M);
+// L = sum over the chunks in order of fmaf(l_s, w_s, L); o = sum over the
+// chunks in order of fmaf(o_s, w_s, o); value = o / L.  The chunk values of
+// one output are loaded in batches of kMergeBatch independent loads.
+constexpr int kMergeBatch = 48;
+
+__global__ void __launch_bounds__(kAqThreads) attn_quant_kernel(const __grid_constant__ AttnQuantArgs aa) {
+    extern __shared__ float msm[];  // [nhc][max_splits] maxima, then weights; [nhc][max_splits] sums; [nhc] L
+    __shared__ float gmax_w[kAqThreads / 32];
+    __shared__ int gsum_w[kAqThreads / 32];
+    const ActQuantArgs& a = aa.q;
+    pdl_trigger();
+    kt_start(a.kt);
+    pdl_wait();
+    kt_waited(a.kt);
+    const int b = blockIdx.y, n = a.n, gs = a.gs, ng = n / gs, hs = aa.head_size;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int k0 = blockIdx.x * kAqThreads, k = k0 + tid;
+    const bool on = k < n;
+    const int nsplit = a.meta[2 * b + 1] / kChunk + 1;
+    float v = 0.0f;
+    if (nsplit == 1) {
+        if (on) v = a.x[(size_t)b * n + k];
+    } else {
+        const int ms = aa.max_splits, ps = hs + 4;
+        const int h0 = k0 / hs, h1 = (min(k0 + kAqThreads, n) - 1) / hs, nhc = h1 - h0 + 1;
+        float* mw = msm;             // [nhc][ms]
+        float* lw = msm + nhc * ms;  // [nhc][ms]
+        float* Ls = lw + nhc * ms;   // [nhc]
+        const float* prow = aa.part + (size_t)b * (n / hs) * ms * ps;
+        for (int i = tid; i < nhc * nsplit; i += kAqThreads) {
+            const int hh = i / nsplit, s2 = i - hh * nsplit;
+            const float2 m_l = __ldcg(reinterpret_cast<const float2*>(prow + ((size_t)(h0 + hh) * ms + s2) * ps));
+            mw[hh * ms + s2] = m_l.x;
+            lw[hh * ms + s2] = m_l.y;
+        }
+        __syncthreads();
+        for (int hh = warp; hh < nhc; hh += kAqThreads / 32) {
+            float M = -FLT_MAX;
+            for (int s2 = lane; s2 < nsplit; s2 += 32) M = fmaxf(M, mw[hh * ms + s2]);
+            M = warp_max(M);
+            for (int s2 = lane; s2 < nsplit; s2 += 32) mw[hh * ms + s2] = lq_expf(mw[hh * ms + s2] - M);
+            __syncwarp();
+            if (lane == 0) {
+                float L = 0.0f;
+                for (int s2 = 0; s2 < nsplit; ++s2) L = fmaf(lw[hh * ms + s2], mw[hh * ms + s2], L);
+                Ls[hh] = L;
+            }
+        }
+        __syncthreads();
+        if (on) {
+            const int hh = k / hs - h0, d = k - (k / hs) * hs;
+            const float* src = prow + (size_t)(h0 + hh) * ms * ps + 4 + d;
+            const float* w = mw + hh * ms;
+            float o = 0.0f;
+            for (int s0 = 0; s0 < nsplit; s0 += kMergeBatch) {
+                float x[kMergeBatch];
+#pragma unroll
+                for (int u = 0; u < kMergeBatch; ++u) x[u] = s0 + u < nsplit ? __ldcg(src + (size_t)(s0 + u) * ps) : 0.0f;
+#pragma unroll
+                for (int u = 0; u < kMergeBatch; ++u)
+                    if (s0 + u < nsplit) o = fmaf(x[u], w[s0 + u], o);
+            }
+            v = o / Ls[hh];
+        }
+    }
+    // quantize as quant_task8 does: group absmax, scale amax / 127, values
+    // quant_div(v, scale) clamped to [-127, 127], group sum of the values
+    const int wpg = gs / 32;  // warps per group
+    const int gw0 = (warp / wpg) * wpg;
+    float amax = warp_max(on ? fabsf(v) : 0.0f);
+    if (lane == 0) gmax_w[warp] = amax;
+    __syncthreads();
+    amax = 0.0f;
+    for (int w2 = 0; w2 < wpg; ++w2) amax = fmaxf(amax, gmax_w[gw0 + w2]);
+    float sc = amax / 127.0f;
+    if (sc == 0.0f) sc = 1e-8f;
+    const float rcp = 1.0f / sc;
+    const int q = on ? max(-127, min(127, quant_div(v, sc, rcp))) : 0;
+    if (on) a.xq[(size_t)b * n + k] = (int8_t)q;
+    int qs = q;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) qs += __shfl_xor_sync(0xffffffffu, qs, o);
+    if (lane == 0) gsum_w[warp] = qs;
+    __syncthreads();
+    if (on && (k & (gs - 1)) == 0) {
+        int tot = 0;
+        for (int w2 = 0; w2 < wpg; ++w2) tot += gsum_w[gw0 + w2];
+        const int g = k / gs;
+        a.xs[(size_t)b * ng + g] = sc;
+        a.xsum[(size_t)b * ng + g] = tot;
+        if (a.xs_t) {
+            const int c = b >> 6, ld = c < a.xs_nfull ? 64 : a.xs_npad_last;
+            a.xs_t[(size_t)c * ng * 64 + (size_t)g * ld + (b & 63)] = sc * a.xs_t_mul;
+        }
+    }
+    kt_end_cta(a.kt);
+}
+
+cudaError_t attn_quant_launch(const AttnQuantArgs& a, cudaStream_t st, bool pdl) {
+    const int n = a.q.n, hs = a.head_size;
+    if (!gs_ok_dev(a.q.gs) || n % a.q.gs || hs < 1 || n % hs || a.max_splits < 1) return cudaErrorInvalidValue;
+    const int nhc = kAqThreads / hs + 2;
+    const size_t smem = sizeof(float) * ((size_t)2 * nhc * a.max_splits + nhc);
+    static size_t set_bytes = 0;
+    if (smem > 48 * 1024 && smem > set_bytes) {
+        cudaError_t e = cudaFuncSetAttribute(attn_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        set_bytes = smem;
+    }
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((n + kAqThreads - 1) / kAqThreads, a.q.nb);
+    cfg.blockDim = dim3(kAqThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attn_quant_kernel, a);
 }
 
 // ---------------------------------------------------------------------------

@@ -2,6 +2,7 @@
 // dependent launch, bounded waits.  Inline PTX from the public PTX ISA.
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace lq {
@@ -89,6 +90,18 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
+// 2-D tiled tensor copy global -> shared (TMA): the box at (x, y) of the
+// tensor map, completion signalled on `bar` as tx bytes.  x * element size
+// must be a multiple of 16 bytes.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                            uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
 // Programmatic dependent launch (PTX griddepcontrol).
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() {
@@ -109,6 +122,13 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// the xor butterfly levels o, o/2, ..., 1 of a warp sum
+__device__ __forceinline__ float warp_sum_below(float v, int o) {
+#pragma unroll
+    for (; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;
 }
 

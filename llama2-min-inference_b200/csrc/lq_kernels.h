@@ -119,6 +119,16 @@ struct ActQuantArgs {
 };
 cudaError_t act_quant_launch(const ActQuantArgs& a, cudaStream_t st, bool pdl);
 
+// The quantizer in front of the wo product: merges the attention kernel's
+// per-chunk partials of every head (or, for a single chunk, reads its
+// normalised output q.x) and quantizes the row.  q.n = heads * head_size.
+struct AttnQuantArgs {
+    ActQuantArgs q;       // mode ignored; x = the attention output [nb][n]
+    const float* part;    // [nb][n / head_size][max_splits][head_size + 4]: m, l, -, -, o
+    int head_size, max_splits;
+};
+cudaError_t attn_quant_launch(const AttnQuantArgs& a, cudaStream_t st, bool pdl);
+
 // Tensor-parallel all-reduce fused into the quantizer that follows a wo / w2
 // product.  Each process owns an exchange region in its own device memory,
 // mapped by every peer (CUDA IPC):

@@ -1,6 +1,7 @@
 // Transformer state (C++ only; opaque in the C ABI).
 #pragma once
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include "lq_host.h"
@@ -38,8 +39,8 @@ struct Transformer {
     float* xqs = nullptr;
     int* xqsum = nullptr;
     float *kc = nullptr, *vc = nullptr;  // [B][L][kv_heads][max_seq][head_size]
-    float* part = nullptr;               // attention partials
-    int* counters = nullptr;             // attention arrival counters
+    alignas(64) CUtensorMap kmap{};      // kc as rows of head_size floats, for the attention kernel
+    float* part = nullptr;               // attention partials [B][heads][max_splits][head_size + 4]
     int* meta = nullptr;                 // [B][token, pos]
     int* next = nullptr;                 // [B] argmax
     int* err = nullptr;                  // device error word

@@ -172,8 +172,10 @@ int alloc_state(Transformer* t) {
     rc = rc ? rc : dalloc(&t->xqsum, (size_t)BP * (maxn / t->gs));
     rc = rc ? rc : dalloc(&t->kc, kv);
     rc = rc ? rc : dalloc(&t->vc, kv);
-    rc = rc ? rc : dalloc(&t->part, (size_t)B * t->nh_l * t->max_splits * (t->head_size + 2));
-    rc = rc ? rc : dalloc(&t->counters, (size_t)B * t->nkv_l);
+    if (!rc && (kv / t->head_size >= (size_t)INT32_MAX ||
+                !lq::kv_tensor_map(&t->kmap, t->kc, t->head_size, kv / t->head_size)))
+        rc = lq_fail(LQ_EUNSUPPORTED, "K-cache tensor map (%zu rows of %d floats)", kv / t->head_size, t->head_size);
+    rc = rc ? rc : dalloc(&t->part, (size_t)B * t->nh_l * t->max_splits * (t->head_size + 4));
     rc = rc ? rc : dalloc(&t->meta, (size_t)2 * B);
     rc = rc ? rc : dalloc(&t->next, (size_t)B);
     rc = rc ? rc : dalloc(&t->err, 1);
@@ -196,8 +198,7 @@ int alloc_state(Transformer* t) {
         cudaError_t e0 = cudaMemcpy(t->rope, tab.data(), tab.size() * sizeof(float2), cudaMemcpyHostToDevice);
         if (e0 != cudaSuccess) return cuda_fail(e0, "rope table");
     }
-    cudaError_t e = cudaMemset(t->counters, 0, (size_t)B * t->nkv_l * sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(t->qg_cnt, 0, (size_t)kQgTiles * sizeof(int));
+    cudaError_t e = cudaMemset(t->qg_cnt, 0, (size_t)kQgTiles * sizeof(int));
     if (e == cudaSuccess) e = cudaMemset(t->xs_t, 0, (size_t)t->xs_ld * (maxn / t->gs) * sizeof(float));
     if (e == cudaSuccess) e = cudaMemset(t->xq, 0, (size_t)BP * maxn);
     if (e == cudaSuccess) e = cudaMemset(t->xqs, 0, (size_t)BP * (maxn / t->gs) * sizeof(float));
@@ -231,7 +232,7 @@ void free_state(Transformer* t) {
     t->pgraph = nullptr;
     t->pgraph_rows = 0;
     void* bufs[] = {t->x, t->q, t->att, t->h1, t->h3, t->xq, t->xqs, t->xqsum, t->logits, t->kc, t->vc,
-                    t->part, t->counters, t->meta, t->next, t->err, t->rope, t->xs_t, t->qg_part, t->qg_cnt,
+                    t->part, t->meta, t->next, t->err, t->rope, t->xs_t, t->qg_part, t->qg_cnt,
                     t->x2, t->ybuf};
     for (void* b : bufs) cudaFree(b);
     t->xs_t = t->qg_part = t->x2 = t->ybuf = nullptr;
@@ -239,7 +240,7 @@ void free_state(Transformer* t) {
     t->x = t->q = t->att = t->h1 = t->h3 = t->logits = t->kc = t->vc = t->part = nullptr;
     t->xq = nullptr;
     t->xqs = nullptr;
-    t->xqsum = t->counters = t->meta = t->next = t->err = nullptr;
+    t->xqsum = t->meta = t->next = t->err = nullptr;
     t->rope = nullptr;
     cudaFreeHost(t->h_logits);
     cudaFreeHost(t->h_meta);
@@ -375,8 +376,8 @@ int forward_launch(Transformer* t, int batch) {
     };
     cudaError_t e;
     // activation quantizer in front of every GEMV (quantize_act, runq.c:345,394,400,412,418)
-    auto quant = [&](int mode, const float* x, int n, const float* rms_w, float* x_out = nullptr,
-                     const float* y = nullptr) -> cudaError_t {
+    auto qargs = [&](int mode, const float* x, int n, const float* rms_w, float* x_out = nullptr,
+                     const float* y = nullptr) -> ActQuantArgs {
         ActQuantArgs q{};
         q.mode = mode;
         q.n = n;
@@ -398,7 +399,11 @@ int forward_launch(Transformer* t, int batch) {
             q.xs_t_mul = kind == LQ_KIND_INT4 ? 0.0625f : 1.0f;
         }
         q.kt = kt_next(t, LQ_TRACE_QUANT);
-        return act_quant_launch(q, st, true);
+        return q;
+    };
+    auto quant = [&](int mode, const float* x, int n, const float* rms_w, float* x_out = nullptr,
+                     const float* y = nullptr) -> cudaError_t {
+        return act_quant_launch(qargs(mode, x, n, rms_w, x_out, y), st, true);
     };
     auto qin = [&](GemvArgs& a) {
         a.in_mode = IN_QUANT;
@@ -485,12 +490,13 @@ int forward_launch(Transformer* t, int batch) {
         if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "qkv gemv");
         // 2. attention (this process's heads)
         AttnArgs at{};
+        at.kmap = t->kmap;
+        at.krow = (kc + l * kv_layer - t->kc) / hs;
         at.q = t->q;
         at.kcache = kc + l * kv_layer;
         at.vcache = vc + l * kv_layer;
         at.out = t->att;
         at.part = t->part;
-        at.counters = t->counters;
         at.meta = t->meta;
         at.err = t->err;
         at.kv_seq_stride = kv_seq;
@@ -504,7 +510,12 @@ int forward_launch(Transformer* t, int batch) {
         at.kt = kt_next(t, LQ_TRACE_ATTENTION);
         if ((e = attention_launch(at, batch, st, true)) != cudaSuccess) return cuda_fail(e, "attention");
         // 3. wo + residual
-        if ((e = quant(IN_F32, t->att, DQ, nullptr)) != cudaSuccess) return cuda_fail(e, "attention output quantize");
+        AttnQuantArgs aq{};
+        aq.q = qargs(IN_F32, t->att, DQ, nullptr);
+        aq.part = t->part;
+        aq.head_size = hs;
+        aq.max_splits = t->max_splits;
+        if ((e = attn_quant_launch(aq, st, true)) != cudaSuccess) return cuda_fail(e, "attention merge + quantize");
         base(a, DQ);
         a.seg[0] = {t->wo.q + (size_t)l * D * rbQ, t->wo.s + (size_t)l * D * ngQ, t->tp ? ywo : xa, D,
                     t->tp ? EPI_STORE : EPI_ADD};

@@ -50,22 +50,75 @@ cudaError_t quantize_act_launch(const float* x, int64_t rows, int64_t n, int gs,
 // Semantics: runq.c:369-391 — per query head h, scores q.k_t / sqrt(hs) for
 // t <= pos, softmax, output sum_t p_t v_t (fp32).  Structure: one CTA per
 // (kv head, chunk of kChunk positions, sequence); the CTA serves all query
-// heads of its kv head (GQA: K/V are read from HBM once).  A CTA writes its
-// unnormalised partial (max, sum, o); the last CTA of a kv head (arrival
-// counter) merges the partials and writes the normalised output.  A single
-// chunk writes the output directly.  The output stays fp32: the wo GEMV
-// quantizes it in its prologue (runq.c:394 order: quantize the normalised
-// output — not v5's unnormalised-scale variant).
+// heads of its kv head (GQA: K/V are read from HBM once) and writes each
+// head's unnormalised partial (max m, sum l, o[hs]).  A single chunk writes
+// the normalised output directly; otherwise the activation quantizer in
+// front of the wo product merges the partials (attn_quant_kernel).  The
+// output stays fp32 until that quantizer (runq.c:394 order: quantize the
+// normalised output — not v5's unnormalised-scale variant).
 
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_constant__ AttnArgs a) {
-    extern __shared__ __align__(16) float asmem[];
+// Butterfly step that halves the values a lane holds: lanes with bit `o` set
+// keep the upper half of in[], the others the lower half, and each adds the
+// half its partner (lane ^ o) sent.  For value i of a lane that kept the
+// lower half the sum is in[i] + partner's in[i]; every sum pairs the same two
+// lane values as a plain xor butterfly over that head would.
+template <int C>
+__device__ __forceinline__ void halve(const float (&in)[C], float (&out)[C / 2], int o, int lane) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < C / 2; ++i) {
+        const float send = up ? in[i] : in[i + C / 2];
+        const float keep = up ? in[i + C / 2] : in[i];
+        out[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+}
+
+// Sum over the 32 lanes of KM values per lane (one per head), as KM xor
+// butterflies (l + l^16, then 8, 4, 2, 1 apart) would each add them.  The
+// head whose sum a lane ends with: head_of_lane<KM>(lane).
+template <int KM>
+__device__ __forceinline__ float multi_warp_sum(const float (&v)[KM], int lane) {
+    if constexpr (KM == 1) {
+        return warp_sum(v[0]);
+    } else {
+        float h[KM / 2];
+        halve<KM>(v, h, 16, lane);
+        if constexpr (KM == 2) {
+            return warp_sum_below(h[0], 8);
+        } else {
+            float g[KM / 4];
+            halve<KM / 2>(h, g, 8, lane);
+            if constexpr (KM == 4) {
+                return warp_sum_below(g[0], 4);
+            } else {
+                static_assert(KM == 8, "KM in {1, 2, 4, 8}");
+                float f[1];
+                halve<2>(g, f, 4, lane);
+                return warp_sum_below(f[0], 2);
+            }
+        }
+    }
+}
+template <int KM>
+__device__ __forceinline__ int head_of_lane(int lane) {
+    // bit 16 picks the upper half of the heads, bit 8 the upper half of the rest, ...
+    return KM == 1 ? 0 : KM == 2 ? (lane >> 4) : KM == 4 ? (lane >> 3) : (lane >> 2);
+}
+
+// NT threads per CTA.  KM = kv_mul when it is 1, 2, 4 or 8 and head_size <=
+// 128 (queries held in registers, the heads of a position reduced together);
+// KM = 0 for any other shape (queries in shared memory, one head at a time).
+// Both keep one arithmetic order.
+template <int NT, int KM>
+__global__ void __launch_bounds__(NT, 1024 / NT) attention_kernel(const __grid_constant__ AttnArgs a) {
+    extern __shared__ __align__(16) unsigned char araw[];
     __shared__ __align__(8) uint64_t kv_bar;
     pdl_trigger();
     kt_start(a.kt);
     const int kvh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
-    const int hs = a.head_size, km = a.kv_mul;
+    const int hs = a.head_size, km = KM ? KM : a.kv_mul;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    constexpr int NW = kAttnThreads / 32;
+    constexpr int NW = NT / 32;
     // the positions were written before the step's first kernel started, so
     // they can be read before waiting for the preceding kernel
     const int pos = a.meta[2 * b + 1];
@@ -74,68 +127,95 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     const int t0 = split * kChunk;
     const int nt = min(kChunk, pos + 1 - t0);
 
-    float* ks = asmem;                  // [kChunk][hs]
-    float* vs = ks + kChunk * hs;       // [kChunk][hs]
-    float* qs = vs + kChunk * hs;       // [km][hs]
-    float* sc = qs + km * hs;           // [km][kChunk]
-    float* ml = sc + km * kChunk;       // [km][2]
+    // K of the chunk in nreg regions of kChunk rows x 128 bytes (dims 32m ..
+    // 32m+31 of every position), each written by one tensor copy with the
+    // 128-byte swizzle: 16-byte chunk c of row t sits at chunk c ^ (t & 7), so
+    // a warp reading one row, or one chunk of 8 consecutive rows, meets no
+    // bank conflict.  The swizzle needs 1024-byte aligned regions.
+    const int nreg = (hs + 31) / 32;
+    unsigned char* kbase = araw + ((1024 - (smem_addr(araw) & 1023u)) & 1023u);
+    float* vs = reinterpret_cast<float*>(kbase + (size_t)nreg * kChunk * 128);  // [kChunk][hs]
+    float* qs = vs + kChunk * hs;          // [km][hs] (KM = 0)
+    float* sc = qs + (KM ? 0 : km * hs);   // [km][kChunk] scores, then weights
+    float* ml = sc + km * kChunk;          // [km][2]
 
-    // K and V of the chunk by two bulk copies (TMA).  A chunk without the
-    // current position holds only earlier steps' keys and values, so its copy
-    // starts before the preceding kernel (which writes position pos) is done.
+    // K by nreg tensor copies, V by one bulk copy (the chunk's positions are
+    // contiguous rows of the cache).  A chunk without the current position
+    // holds only earlier steps' keys and values, so its copies start before
+    // the preceding kernel (which writes position pos) is done.
     const size_t cbase = (size_t)b * a.kv_seq_stride + ((size_t)kvh * a.max_seq + t0) * hs;
-    const uint32_t bytes = (uint32_t)(nt * hs * sizeof(float));
+    const uint32_t vbytes = (uint32_t)(nt * hs * sizeof(float));
     if (tid == 0) {
         mbar_init(&kv_bar, 1);
         fence_mbar_init();
         if (t0 + nt - 1 == pos) pdl_wait();
         const uint64_t pol = l2_evict_first_policy();
-        mbar_arrive_expect_tx(&kv_bar, 2 * bytes);
-        bulk_g2s(ks, a.kcache + cbase, bytes, &kv_bar, pol);
-        bulk_g2s(vs, a.vcache + cbase, bytes, &kv_bar, pol);
+        mbar_arrive_expect_tx(&kv_bar, (uint32_t)nreg * kChunk * 128 + vbytes);
+        const int row = (int)(a.krow + (int64_t)(cbase / hs));
+        for (int m = 0; m < nreg; ++m)
+            tma_load_2d(kbase + (size_t)m * kChunk * 128, &a.kmap, 128 * m, row, &kv_bar, pol);
+        bulk_g2s(vs, a.vcache + cbase, vbytes, &kv_bar, pol);
     }
     pdl_wait();
     kt_waited(a.kt);
     const float* qg = a.q + (size_t)b * a.q_stride + (size_t)kvh * km * hs;
-    for (int i = tid; i < km * hs; i += kAttnThreads) qs[i] = qg[i];
-    __syncthreads();  // also orders the barrier's initialisation before the waits below
-    const bool landed = mbar_wait(&kv_bar, 0, a.err, DEV_TIMEOUT_FULL);
-    if (!__syncthreads_and(landed)) {
-        // give up on this chunk; confirm the copies before the CTA's shared memory is released
-        if (tid == 0) mbar_wait(&kv_bar, 0, a.err, DEV_TIMEOUT_DRAIN);
-        return;
-    }
+    // dim lane + 32m of row t: region m, 16-byte chunk lane / 4 (swizzled), word lane % 4
+    auto kval = [&](int t, int m) {
+        return *reinterpret_cast<const float*>(kbase + (size_t)m * kChunk * 128 + t * 128 +
+                                               ((((lane >> 2) ^ (t & 7)) << 4) | ((lane & 3) << 2)));
+    };
 
-    // scores: warp per position, lanes over dims.  Four positions at a time per
-    // warp: independent dot products and reductions interleave (each one in
-    // the same order as alone).
+    // scores q_j . k_t / sqrt(hs), the reference's warp-reduction order: 32
+    // partial sums (partial l takes dims l, l+32, ... in increasing order with
+    // fmaf; here lane l), added as an xor butterfly over the 32 lanes.  A warp
+    // per position.
     const float rs = sqrtf((float)hs);
-    constexpr int U = 4;
-    for (int t0w = warp; t0w < nt; t0w += U * NW) {
-        for (int j = 0; j < km; ++j) {
-            const float* qj = qs + j * hs;
-            float p[U];
+    if constexpr (KM > 0) {
+        float qr[KM][4];
 #pragma unroll
-            for (int u = 0; u < U; ++u) p[u] = 0.0f;
-#pragma unroll 4
-            for (int i = lane; i < hs; i += 32) {
-                const float qv = qj[i];
+        for (int j = 0; j < KM; ++j)
 #pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int t = t0w + u * NW;
-                    if (t < nt) p[u] = fmaf(qv, ks[t * hs + i], p[u]);
+            for (int m = 0; m < 4; ++m) qr[j][m] = lane + 32 * m < hs ? qg[j * hs + lane + 32 * m] : 0.0f;
+        __syncthreads();  // orders the barrier's initialisation before the waits below
+        const bool landed = mbar_wait(&kv_bar, 0, a.err, DEV_TIMEOUT_FULL);
+        if (!__syncthreads_and(landed)) {
+            // give up on this chunk; confirm the copies before the CTA's shared memory is released
+            if (tid == 0) mbar_wait(&kv_bar, 0, a.err, DEV_TIMEOUT_DRAIN);
+            return;
+        }
+        const int jl = head_of_lane<KM>(lane);
+        const bool writer = (lane & (32 / KM - 1)) == 0;
+        for (int t = warp; t < nt; t += NW) {
+            float acc[KM];
+#pragma unroll
+            for (int j = 0; j < KM; ++j) acc[j] = 0.0f;
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                if (lane + 32 * m < hs) {
+                    const float kv = kval(t, m);
+#pragma unroll
+                    for (int j = 0; j < KM; ++j) acc[j] = fmaf(qr[j][m], kv, acc[j]);
                 }
             }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-                for (int u = 0; u < U; ++u) p[u] += __shfl_xor_sync(0xffffffffu, p[u], o);
-            if (lane == 0)
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const int t = t0w + u * NW;
-                    if (t < nt) sc[j * kChunk + t] = p[u] / rs;
-                }
+            const float dot = multi_warp_sum<KM>(acc, lane);
+            if (writer) sc[jl * kChunk + t] = dot / rs;
+        }
+    } else {
+        for (int i = tid; i < km * hs; i += NT) qs[i] = qg[i];
+        __syncthreads();
+        const bool landed = mbar_wait(&kv_bar, 0, a.err, DEV_TIMEOUT_FULL);
+        if (!__syncthreads_and(landed)) {
+            if (tid == 0) mbar_wait(&kv_bar, 0, a.err, DEV_TIMEOUT_DRAIN);
+            return;
+        }
+        for (int t = warp; t < nt; t += NW) {
+            for (int j = 0; j < km; ++j) {
+                float acc = 0.0f;
+                for (int m = 0; m < nreg; ++m)
+                    if (lane + 32 * m < hs) acc = fmaf(qs[j * hs + lane + 32 * m], kval(t, m), acc);
+                acc = warp_sum(acc);
+                if (lane == 0) sc[j * kChunk + t] = acc / rs;
+            }
         }
     }
     __syncthreads();
@@ -157,97 +237,95 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
         }
     }
     __syncthreads();
-    // o[j][d] = sum_t p[j][t] * v[t][d]
+    // o[j][d] = sum_t p[j][t] * v[t][d] in position order with fmaf.  The
+    // unnormalised partial of head j: [m, l, -, -, o[hs]] (o 16-byte aligned)
     float* out = a.out + (size_t)b * a.q_stride + (size_t)kvh * km * hs;
     const int hq0 = kvh * km;
-    for (int i = tid; i < km * hs; i += kAttnThreads) {
-        const int j = i / hs, d = i - j * hs;
-        const float* pj = sc + j * kChunk;
-        float o = 0.0f;
-#pragma unroll 8
-        for (int t = 0; t < nt; ++t) o = fmaf(pj[t], vs[t * hs + d], o);
-        if (nsplit == 1) {
-            out[i] = o / ml[2 * j + 1];
-        } else {
-            float* part = a.part + (((size_t)b * a.n_heads + hq0 + j) * a.max_splits + split) * (hs + 2);
-            part[2 + d] = o;
-            if (d == 0) {
-                part[0] = ml[2 * j];
-                part[1] = ml[2 * j + 1];
-            }
-        }
-    }
-    if (nsplit == 1) {
-        kt_end_cta(a.kt);
-        return;
-    }
-    // last-arriving CTA of this kv head merges the partials
-    __threadfence();
-    __syncthreads();
-    __shared__ int is_last;
-    if (tid == 0) {
-        int* cnt = a.counters + (size_t)b * a.n_kv_heads + kvh;
-        is_last = atomicAdd(cnt, 1) == nsplit - 1;
-        if (is_last) *cnt = 0;  // re-arm for the next step
-    }
-    __syncthreads();
-    if (!is_last) {
-        kt_end_cta(a.kt);
-        return;
-    }
-    __threadfence();
-    // The partials of a group of heads are first copied into shared memory
-    // (the K / V chunk buffers are free by now) by every thread at once, so
-    // the merge waits for one round of L2 loads, not one per chunk; the merge
-    // arithmetic itself is unchanged: M = max over the chunks, then L and o
-    // accumulated with fmaf in chunk order.
-    const int per_head = nsplit * (hs + 2);
-    const int cap = 2 * kChunk * hs;                    // floats of the K and V buffers
-    const int hb = cap / per_head < 1 ? 1 : (cap / per_head < km ? cap / per_head : km);
-    const bool staged = per_head <= cap;
-    for (int j0 = 0; j0 < km; j0 += hb) {
-        const int nh = km - j0 < hb ? km - j0 : hb;
-        if (staged) {
-            __syncthreads();  // the previous group's reads of the buffer are done
-            for (int hh = 0; hh < nh; ++hh) {
-                const float* src = a.part + (((size_t)b * a.n_heads + hq0 + j0 + hh) * a.max_splits) * (hs + 2);
-                float* dst = ks + hh * per_head;
-                for (int i = tid; i < per_head; i += kAttnThreads) dst[i] = __ldcg(src + i);
-            }
-            __syncthreads();
-        }
-        for (int i = tid; i < nh * hs; i += kAttnThreads) {
-            const int jj = i / hs, d = i - jj * hs, j = j0 + jj;
-            const float* base = staged ? ks + jj * per_head
-                                       : a.part + (((size_t)b * a.n_heads + hq0 + j) * a.max_splits) * (hs + 2);
-            float M = -FLT_MAX;
-#pragma unroll 8
-            for (int s = 0; s < nsplit; ++s) M = fmaxf(M, base[(size_t)s * (hs + 2)]);
-            float L = 0.0f, o = 0.0f;
+    auto partial = [&](int j) {
+        return a.part + (((size_t)b * a.n_heads + hq0 + j) * a.max_splits + split) * (hs + 4);
+    };
+    if (KM >= 2) {
+        // a thread per 4 dims of 2 heads
+        const int nd4 = hs / 4;
+        for (int i = tid; i < nd4 * (km / 2); i += NT) {
+            const int jp = i / nd4, d = (i - jp * nd4) * 4, j = 2 * jp;
+            const float* p0 = sc + j * kChunk;
+            const float* p1 = p0 + kChunk;
+            float o[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) o[u] = 0.0f;
 #pragma unroll 4
-            for (int s = 0; s < nsplit; ++s) {
-                const float* ps = base + (size_t)s * (hs + 2);
-                const float w = lq_expf(ps[0] - M);
-                L = fmaf(ps[1], w, L);
-                o = fmaf(ps[2 + d], w, o);
+            for (int t = 0; t < nt; ++t) {
+                const float4 v = *reinterpret_cast<const float4*>(vs + t * hs + d);
+                const float a0 = p0[t], a1 = p1[t];
+                o[0] = fmaf(a0, v.x, o[0]);
+                o[1] = fmaf(a0, v.y, o[1]);
+                o[2] = fmaf(a0, v.z, o[2]);
+                o[3] = fmaf(a0, v.w, o[3]);
+                o[4] = fmaf(a1, v.x, o[4]);
+                o[5] = fmaf(a1, v.y, o[5]);
+                o[6] = fmaf(a1, v.z, o[6]);
+                o[7] = fmaf(a1, v.w, o[7]);
             }
-            out[j * hs + d] = o / L;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float* oh = o + 4 * h;
+                if (nsplit == 1) {
+                    const float L = ml[2 * (j + h) + 1];
+                    *reinterpret_cast<float4*>(out + (j + h) * hs + d) =
+                        make_float4(oh[0] / L, oh[1] / L, oh[2] / L, oh[3] / L);
+                } else {
+                    float* pp = partial(j + h);
+                    *reinterpret_cast<float4*>(pp + 4 + d) = make_float4(oh[0], oh[1], oh[2], oh[3]);
+                    if (d == 0) {
+                        pp[0] = ml[2 * (j + h)];
+                        pp[1] = ml[2 * (j + h) + 1];
+                    }
+                }
+            }
+        }
+    } else {
+        // a thread per (head, dim)
+        for (int i = tid; i < km * hs; i += NT) {
+            const int j = i / hs, d = i - j * hs;
+            const float* pj = sc + j * kChunk;
+            float o = 0.0f;
+#pragma unroll 8
+            for (int t = 0; t < nt; ++t) o = fmaf(pj[t], vs[t * hs + d], o);
+            if (nsplit == 1) {
+                out[i] = o / ml[2 * j + 1];
+            } else {
+                float* pp = partial(j);
+                pp[4 + d] = o;
+                if (d == 0) {
+                    pp[0] = ml[2 * j];
+                    pp[1] = ml[2 * j + 1];
+                }
+            }
         }
     }
     kt_end_cta(a.kt);
 }
 
 size_t attention_smem_bytes(int head_size, int kv_mul) {
-    return sizeof(float) * ((size_t)2 * kChunk * head_size + (size_t)kv_mul * head_size +
-                            (size_t)kv_mul * kChunk + 2 * (size_t)kv_mul);
+    const size_t kbytes = (size_t)((head_size + 31) / 32) * kChunk * 128;  // swizzled K regions
+    return 1024 + kbytes +
+           sizeof(float) * ((size_t)kChunk * head_size + (size_t)kv_mul * head_size + (size_t)kv_mul * kChunk +
+                            2 * (size_t)kv_mul);
 }
 
-cudaError_t attention_launch(const AttnArgs& a, int batch, cudaStream_t st, bool pdl) {
+namespace {
+template <int NT, int KM>
+cudaError_t launch_attention(const AttnArgs& a, int batch, cudaStream_t st, bool pdl) {
     const size_t smem = attention_smem_bytes(a.head_size, a.kv_mul);
+    auto kern = attention_kernel<NT, KM>;
     static size_t set_bytes = 0;
-    if (smem > 48 * 1024 && smem > set_bytes) {
-        cudaError_t e =
-            cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (smem > set_bytes) {
+        // the largest shared-memory carveout: with the default the driver may
+        // keep one CTA per SM where two fit
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
         if (e != cudaSuccess) return e;
         set_bytes = smem;
     }
@@ -256,12 +334,27 @@ cudaError_t attention_launch(const AttnArgs& a, int batch, cudaStream_t st, bool
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_kv_heads, a.max_splits, batch);
-    cfg.blockDim = dim3(kAttnThreads);
+    cfg.blockDim = dim3(NT);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, attention_kernel, a);
+    return cudaLaunchKernelEx(&cfg, kern, a);
+}
+}  // namespace
+
+cudaError_t attention_launch(const AttnArgs& a, int batch, cudaStream_t st, bool pdl) {
+    if (a.head_size % 4) return cudaErrorInvalidValue;
+    if (a.head_size <= 128) {
+        switch (a.kv_mul) {
+        case 1: return launch_attention<256, 1>(a, batch, st, pdl);
+        case 2: return launch_attention<256, 2>(a, batch, st, pdl);
+        case 4: return launch_attention<512, 4>(a, batch, st, pdl);
+        case 8: return launch_attention<512, 8>(a, batch, st, pdl);
+        default: break;
+        }
+    }
+    return launch_attention<512, 0>(a, batch, st, pdl);
 }
 
 // ---------------------------------------------------------------------------

@@ -46,6 +46,7 @@
 #include "lq_device.cuh"
 #include "lq_epilogue.cuh"
 #include "lq_kernels.h"
+#include "lq_ops.h"
 
 namespace lq {
 
@@ -83,15 +84,6 @@ struct QgemmArgs {
 };
 
 // ---- PTX wrappers (public PTX ISA: tcgen05, cp.async.bulk.tensor) --------
-
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
-                                            uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(smem_addr(dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_addr(bar)), "l"(policy)
-        : "memory");
-}
 
 __device__ __forceinline__ uint64_t l2_evict_last_policy() {
     uint64_t p;
@@ -794,6 +786,12 @@ cudaError_t qgemm_launch(const GemvArgs& a, int kind, const float* xs_t, int xs_
     const int64_t W = (int64_t)tiles * q.kst;
     const int grid = (int)(W < num_sms ? W : num_sms);
     return kind == 8 ? launch_kind<8>(q, npad, mult, st, pdl, grid) : launch_kind<4>(q, npad, mult, st, pdl, grid);
+}
+
+bool kv_tensor_map(CUtensorMap* m, const float* kcache, int head_size, uint64_t rows) {
+    if (!get_encoder()) return false;
+    const uint64_t row = (uint64_t)head_size * sizeof(float);
+    return make_map(m, kcache, row, rows, row, 128, kChunk, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace lq
