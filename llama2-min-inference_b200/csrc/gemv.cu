@@ -1183,13 +1183,6 @@ __global__ void __launch_bounds__(1024) peer_add_quant_kernel(const __grid_const
         const uint32_t e = *reinterpret_cast<volatile const uint32_t*>(&pa.counters[0]) + 1u;
         s_call = e;
         __threadfence();
-        // publish: the previous kernel (this process's partial) completed
-        // before griddepcontrol.wait returned, so any CTA may order it before
-        // the flag; every CTA stores the same value, so none waits on another
-        // CTA being scheduled
-        fence_acq_rel_sys();
-        for (int p = 0; p < pa.tp_size; ++p)
-            if (p != pa.tp_rank) st_release_sys(pa.peer_flag[p], e);
         // the last CTA to read the call number advances it for the next call
         if (atomicAdd(&pa.counters[1], 1u) == gridDim.y - 1) {
             pa.counters[1] = 0;
@@ -1199,55 +1192,50 @@ __global__ void __launch_bounds__(1024) peer_add_quant_kernel(const __grid_const
     __syncthreads();
     const uint32_t e = s_call;
     // once a wait has given up (this call or an earlier one of the step), the
-    // step's result is void: skip further waits so the host hears of it
-    // after one limit, not one per call
-    const bool failed = *reinterpret_cast<volatile const int*>(pa.err) != 0;
-    if (ctid < pa.tp_size && ctid != pa.tp_rank && !failed) {
-        // bounded wait for peer ctid's partial of call e
-        const uint32_t* f = pa.my_flags + ctid;
-        const uint64_t limit = pa.wait_ns ? pa.wait_ns : kWaitLimitNs;
-        if ((int)(ld_acquire_sys(f) - e) < 0) {
-            const uint64_t t0 = globaltimer();
-            for (uint32_t i = 1;; ++i) {
-                if ((int)(ld_acquire_sys(f) - e) >= 0) break;
-                if ((i & 63u) == 0 && (globaltimer() - t0 > limit ||
-                                        *reinterpret_cast<volatile const int*>(pa.err) != 0)) {
-                    set_err(pa.err, DEV_TIMEOUT_PEER);
-                    break;
-                }
-            }
-        }
-    }
-    __syncthreads();
-    // y = sum of the partials in rank order, x_out = x + y (8 values per thread)
+    // step's result is void: no further waits, so the host hears of it after
+    // one limit, not one per call
+    bool failed = *reinterpret_cast<volatile const int*>(pa.err) != 0;
+    const uint64_t limit = pa.wait_ns ? pa.wait_ns : kWaitLimitNs;
+    // y = sum of the processes' partials in rank order, x_out = x + y (8
+    // values per thread); each process's 8 words are polled until all carry
+    // this call's number
     const int task = ctid;
     const bool on = task < n / 8;
     const int k0 = task * 8;
     const size_t off = (size_t)b * n + k0;
     float v[8];
     if (on) {
-        // every peer's loads of one half (4 values) are issued before the
-        // first add, so the NVLink round trips overlap; the adds run in rank order
-        float4 yh[2];
+        float y[8];
+        for (int p = 0; p < pa.tp_size; ++p) {
+            const uint64_t* src = pa.slot + ((size_t)p * pa.ll_rows + b) * n + k0;
+            uint64_t wd[8];
+            uint64_t t0 = 0;
+            for (uint32_t it = 0;; ++it) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-            float4 z[kTpMax];
+                for (int h = 0; h < 4; ++h) ld_relaxed_sys_v2(src + 2 * h, wd[2 * h], wd[2 * h + 1]);
+                bool ready = true;
 #pragma unroll
-            for (int p = 0; p < kTpMax; ++p)
-                if (p < pa.tp_size) z[p] = ld_volatile_f4(pa.peer_slot[p] + off + 4 * h);
-            float4 y = z[0];
-#pragma unroll
-            for (int p = 1; p < kTpMax; ++p)
-                if (p < pa.tp_size) {
-                    y.x += z[p].x; y.y += z[p].y; y.z += z[p].z; y.w += z[p].w;
+                for (int i = 0; i < 8; ++i) ready = ready && (uint32_t)(wd[i] >> 32) == e;
+                if (ready || failed) break;
+                if (it == 0) t0 = globaltimer();
+                if ((it & 15u) == 15u) {
+                    failed = *reinterpret_cast<volatile const int*>(pa.err) != 0;
+                    if (!failed && globaltimer() - t0 > limit) {
+                        set_err(pa.err, DEV_TIMEOUT_PEER);
+                        failed = true;
+                    }
                 }
-            yh[h] = y;
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float z = __uint_as_float((uint32_t)wd[i]);
+                y[i] = p == 0 ? z : y[i] + z;
+            }
         }
-        const float4 y0 = yh[0], y1 = yh[1];
         const float4 x0 = *reinterpret_cast<const float4*>(a.x + off);
         const float4 x1 = *reinterpret_cast<const float4*>(a.x + off + 4);
-        v[0] = x0.x + y0.x; v[1] = x0.y + y0.y; v[2] = x0.z + y0.z; v[3] = x0.w + y0.w;
-        v[4] = x1.x + y1.x; v[5] = x1.y + y1.y; v[6] = x1.z + y1.z; v[7] = x1.w + y1.w;
+        v[0] = x0.x + y[0]; v[1] = x0.y + y[1]; v[2] = x0.z + y[2]; v[3] = x0.w + y[3];
+        v[4] = x1.x + y[4]; v[5] = x1.y + y[5]; v[6] = x1.z + y[6]; v[7] = x1.w + y[7];
         const float4 r0 = make_float4(v[0], v[1], v[2], v[3]), r1 = make_float4(v[4], v[5], v[6], v[7]);
         *reinterpret_cast<float4*>(a.x_out + off) = r0;
         *reinterpret_cast<float4*>(a.x_out + off + 4) = r1;
@@ -1281,7 +1269,7 @@ __global__ void __launch_bounds__(1024) peer_add_quant_kernel(const __grid_const
 cudaError_t peer_add_quant_launch(const PeerAddArgs& a, cudaStream_t st, bool pdl) {
     const int n = a.q.n;
     if (!gs_ok_dev(a.q.gs) || n % a.q.gs || n % 8 || n > kPeerMaxN || a.tp_size < 1 || a.tp_size > kTpMax ||
-        a.q.nb < 1 || a.q.nb > kTpMaxRows)
+        a.q.nb < 1 || a.q.nb > a.ll_rows || !a.slot || !a.counters)
         return cudaErrorInvalidValue;
     const int threads = kAqThreads * ((n / 8 + kAqThreads - 1) / kAqThreads);
     cudaLaunchAttribute attr[1];

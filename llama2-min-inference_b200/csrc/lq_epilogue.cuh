@@ -3,6 +3,7 @@
 // added to the residual stream, rotated (RoPE) into q or the K cache,
 // written to the V cache, or combined with its w3 partner (SwiGLU).
 #pragma once
+#include "lq_device.cuh"
 #include "lq_kernels.h"
 #include "lq_math.h"
 
@@ -46,6 +47,18 @@ __device__ __forceinline__ void finish_rows(const GemvArgs& a, const GemvSeg& g,
             float* y = g.y + (size_t)b * a.y_stride;
             y[r] = v0;
             y[r + 1] = v1;
+        } break;
+        case EPI_PUSH: {
+            // (call << 32) | bits(v) into row (own rank, b) of every process's slot
+            const uint64_t e = (uint64_t)(*a.ll_call + 1u) << 32;
+            const uint64_t w0 = e | __float_as_uint(v0), w1 = e | __float_as_uint(v1);
+            const size_t off = ((size_t)a.ll_rank * a.ll_rows + a.ll_row0 + b) * a.y_stride + r;
+            for (int p = 0; p < a.ll_tp; ++p) {
+                if (has2)
+                    st_relaxed_sys_v2(a.ll[p] + off, w0, w1);  // r even, y_stride even: 16-byte aligned
+                else
+                    st_relaxed_sys_u64(a.ll[p] + off, w0);
+            }
         } break;
         case EPI_ROPE_KCACHE:
         case EPI_VCACHE: {

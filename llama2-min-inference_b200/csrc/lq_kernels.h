@@ -13,6 +13,7 @@ enum Epilogue : int {
     EPI_ROPE_KCACHE = 3,  // rotary pair of the key, stored to the K cache at pos
     EPI_VCACHE = 4,       // value stored to the V cache at pos
     EPI_SWIGLU = 5,       // paired tensors: y[r] = silu(v1) * v3 (runq.c:405-410)
+    EPI_PUSH = 6,         // tensor-parallel partial, pushed to every process's exchange slot (PeerAddArgs)
 };
 
 // Where the int8 activation comes from (the GEMV prologue builds it in
@@ -24,6 +25,8 @@ enum InputMode : int {
     IN_RMSNORM_EMB = 3,  // x = emb[token] (CTA 0 also writes it to x_out), then as IN_RMSNORM
     IN_ADD_RMSNORM = 4,  // x = x + y (CTA 0 also writes it to x_out), then as IN_RMSNORM (activation quantizer only)
 };
+
+constexpr int kTpMax = 8;  // tensor-parallel processes
 
 struct GemvSeg {
     const uint8_t* wq;  // packed weights [rows, row_bytes]
@@ -67,6 +70,11 @@ struct GemvArgs {
     int* err;
     uint64_t* trace;  // optional per-CTA phase timestamps (globaltimer ns), [grid][4]; null = off
     uint64_t* kt;     // optional step-trace stamps of this launch (lq_device.cuh kt_*); null = off
+    // EPI_PUSH: the slot of every process (rank order), this process's call
+    // counter, and the slot geometry (row of batch row b: ll_row0 + b)
+    uint64_t* ll[kTpMax];
+    const uint32_t* ll_call;
+    int ll_tp, ll_rank, ll_rows, ll_row0;
     // schedule (filled by the planner)
     int split;       // 0: stages of whole rows; 1: stages are slices of one row
     int stage_rows;  // rows per stage (whole-row mode)
@@ -130,35 +138,33 @@ struct AttnQuantArgs {
 cudaError_t attn_quant_launch(const AttnQuantArgs& a, cudaStream_t st, bool pdl);
 
 // Tensor-parallel all-reduce fused into the quantizer that follows a wo / w2
-// product.  Each process owns an exchange region in its own device memory,
-// mapped by every peer (CUDA IPC):
-//   flags[kTpMax] (uint32, one per peer: the last call whose partial that
-//   peer has ready), counters[2] (this process only: calls done, CTAs
-//   arrived), then two partial slots of [kTpMaxRows][dim] fp32.
-// The products write their partial into this process's slot (wo: slot 0,
-// w2: slot 1, so the slots alternate call by call).  The quantizer then
-// publishes "partial ready for call e" to every peer, waits (bounded) until
-// every peer has published call e, and reads each peer's partial over
-// NVLink: y = ((y_0 + y_1) + y_2) ... in rank order on every process, x_out
-// = x + y, then rmsnorm + quantize exactly like act_quant_kernel's
-// IN_ADD_RMSNORM (same summation orders), so for two processes the result
-// equals the NCCL all-reduce path bit for bit.
-// A slot is rewritten two calls later, only after the writer has seen every
-// peer publish the call in between, which each peer does only after it has
-// finished reading the slot.
-constexpr int kTpMax = 8;
-constexpr int kTpMaxRows = 1024;
-constexpr int kXrFlagsBytes = 256;     // flags, padded
+// product (low-latency protocol: every value travels with its call number).
+// Each process owns an exchange region in its own device memory, mapped by
+// every peer (CUDA IPC): counters[2] (calls done, CTAs arrived), then two
+// slots of [tp][ll_rows][dim] 64-bit words.  The wo (slot 0) and w2 (slot 1)
+// products push each partial value v of row b, column r as the word
+// (call << 32) | bits(v) into row (own rank, b) of that slot of EVERY
+// process (EPI_PUSH, relaxed system-scope stores over NVLink; the call is
+// counters[0] + 1).  The quantizer polls its own slot until every word of
+// every rank carries the call number, sums y = ((y_0 + y_1) + y_2) ... in
+// rank order, x_out = x + y, then rmsnorm + quantize exactly like
+// act_quant_kernel's IN_ADD_RMSNORM (same summation orders), so for two
+// processes the result equals the NCCL all-reduce path bit for bit.  No
+// flag and no second NVLink round trip: a word is ready when it arrives.
+// A slot is rewritten two calls later: a process pushes call c + 2 only
+// after its quantizer finished call c + 1, which needed every peer's push
+// of c + 1, which each peer makes only after its quantizer finished reading
+// call c.  Waits are bounded (wait_ns); a wait that gives up sets the error
+// word and the later calls of the step skip their waits.
 constexpr int kXrCountersBytes = 256;  // counters, padded
 struct PeerAddArgs {
     ActQuantArgs q;                    // mode IN_ADD_RMSNORM fields except y
-    const float* peer_slot[kTpMax];    // this call's slot of every process (rank order; own one included)
-    uint32_t* peer_flag[kTpMax];       // flags[tp_rank] in every peer's region (own entry unused)
-    const uint32_t* my_flags;          // this process's flags[kTpMax]
+    const uint64_t* slot;              // this process's slot of the call: [tp][ll_rows][n] words
+    int ll_rows;
     uint32_t* counters;                // this process's counters[2]
     int tp_rank, tp_size;
     int* err;
-    uint64_t wait_ns;                  // limit of the wait for the peers' flags (0: the default 2 s)
+    uint64_t wait_ns;                  // limit of the wait for the peers' words (0: the default 2 s)
 };
 cudaError_t peer_add_quant_launch(const PeerAddArgs& a, cudaStream_t st, bool pdl);
 

@@ -41,8 +41,21 @@ namespace {
 
 int64_t rbytes(int64_t cols, int kind) { return kind == LQ_KIND_INT8 ? cols : cols / 2; }
 
-// one partial slot of the peer all-reduce exchange region: [kTpMaxRows][dim] fp32
-size_t xr_slot_bytes(const Transformer* t) { return (size_t)lq::kTpMaxRows * t->c.dim * sizeof(float); }
+
+constexpr int kPromptRows = 64;  // prompt tokens per prefill step (forward_prompt)
+
+// activation rows of the step buffers: max(max_batch, kPromptRows) (a
+// prompt chunk is up to kPromptRows rows of one sequence)
+int act_rows(const Transformer* t) { return t->max_batch > kPromptRows ? t->max_batch : kPromptRows; }
+
+// one slot of the peer all-reduce exchange region: [tp][act_rows][dim] 64-bit words
+size_t xr_slot_bytes(const Transformer* t) {
+    return (size_t)t->tp_size * act_rows(t) * t->c.dim * sizeof(uint64_t);
+}
+// slot k of the exchange region at `base` (this process's or a peer's mapping)
+uint64_t* xr_slot(const Transformer* t, void* base, int k) {
+    return reinterpret_cast<uint64_t*>(static_cast<char*>(base) + lq::kXrCountersBytes + k * xr_slot_bytes(t));
+}
 
 // NCCL, opened on first use: the copy a host framework already loaded
 // (torch's) when there is one, else the system's libnccl.so.2
@@ -77,7 +90,6 @@ const Nccl* nccl() {
 }
 
 constexpr int kQgTiles = 8192;  // arrival counters: tiles of the largest launch (vocab / 128)
-constexpr int kPromptRows = 64;  // prompt tokens per prefill step (forward_prompt)
 
 int alloc_q(QW& w, int64_t rows, int64_t cols, int gs, int kind) {
     w.rows = rows;
@@ -142,7 +154,7 @@ int check_config(const Config* c, int gs, int tp_size = 1) {
 // of one sequence)
 int alloc_state(Transformer* t) {
     const Config& c = t->c;
-    const int B = t->max_batch > kPromptRows ? t->max_batch : kPromptRows;  // activation rows
+    const int B = act_rows(t);  // activation rows
     t->head_size = c.dim / c.n_heads;
     t->kv_mul = c.n_heads / c.n_kv_heads;
     t->nh_l = c.n_heads / t->tp_size;
@@ -279,6 +291,7 @@ cudaError_t product_rows(Transformer* t, const GemvArgs& a, int batch, cudaStrea
             c.meta = a.meta + 2 * b0;
             for (int i = 0; i < c.nseg; ++i)
                 if (c.seg[i].y) c.seg[i].y += (size_t)b0 * a.y_stride;
+            c.ll_row0 = a.ll_row0 + b0;
             if (c.kcache) c.kcache += (size_t)b0 * a.kv_seq_stride;
             if (c.vcache) c.vcache += (size_t)b0 * a.kv_seq_stride;
             // this chunk's scale table: [ng][npad] at chunk offset ng * 64
@@ -310,6 +323,7 @@ cudaError_t gemv_rows(Transformer* t, const GemvArgs& a, int kind, int batch, cu
         c.meta = a.meta + 2 * b0;
         for (int i = 0; i < c.nseg; ++i)
             if (c.seg[i].y) c.seg[i].y += (size_t)b0 * a.y_stride;
+        c.ll_row0 = a.ll_row0 + b0;
         if (c.kcache) c.kcache += (size_t)b0 * a.kv_seq_stride;
         if (c.vcache) c.vcache += (size_t)b0 * a.kv_seq_stride;
         c.kt = kt_next(t, LQ_TRACE_GEMV);
@@ -424,10 +438,6 @@ int forward_launch(Transformer* t, int batch) {
     // peer all-reduce: wo writes its partial to slot 0 of this process's
     // exchange region, w2 to slot 1; the next quantizer reduces over the peers
     const bool peer = t->tp_size > 1 && !t->tp_nccl;
-    auto slot = [&](int k) -> float* {
-        return reinterpret_cast<float*>(static_cast<char*>(t->xr) + kXrFlagsBytes + kXrCountersBytes +
-                                        k * xr_slot_bytes(t));
-    };
     auto add_quant = [&](const float* x, const float* rms_w, float* x_out, int k) -> cudaError_t {
         if (!peer) return quant(IN_ADD_RMSNORM, x, D, rms_w, x_out, t->ybuf);
         PeerAddArgs p{};
@@ -448,13 +458,9 @@ int forward_launch(Transformer* t, int batch) {
             p.q.xs_npad_last = batch % 64 ? qgemm_npad(batch % 64) : 64;
             p.q.xs_t_mul = kind == LQ_KIND_INT4 ? 0.0625f : 1.0f;
         }
-        for (int r = 0; r < t->tp_size; ++r) {
-            char* base = static_cast<char*>(t->xr_peer[r]);
-            p.peer_slot[r] = reinterpret_cast<const float*>(base + kXrFlagsBytes + kXrCountersBytes + k * xr_slot_bytes(t));
-            p.peer_flag[r] = reinterpret_cast<uint32_t*>(base) + t->tp_rank;
-        }
-        p.my_flags = static_cast<const uint32_t*>(t->xr);
-        p.counters = reinterpret_cast<uint32_t*>(static_cast<char*>(t->xr) + kXrFlagsBytes);
+        p.slot = xr_slot(t, t->xr, k);
+        p.ll_rows = act_rows(t);
+        p.counters = static_cast<uint32_t*>(t->xr);
         p.tp_rank = t->tp_rank;
         p.tp_size = t->tp_size;
         p.err = t->err;
@@ -462,8 +468,18 @@ int forward_launch(Transformer* t, int batch) {
         p.q.kt = kt_next(t, LQ_TRACE_ALLREDUCE);
         return peer_add_quant_launch(p, st, true);
     };
-    float* ywo = peer ? slot(0) : t->ybuf;  // where the partial products go
-    float* yw2 = peer ? slot(1) : t->ybuf;
+    // the wo / w2 products under the peer all-reduce: partial values pushed to
+    // slot k of every process's exchange region
+    auto push_to = [&](GemvArgs& a, int k) {
+        a.seg[0].epi = EPI_PUSH;
+        a.seg[0].y = nullptr;
+        for (int r = 0; r < t->tp_size; ++r) a.ll[r] = xr_slot(t, t->xr_peer[r], k);
+        a.ll_call = static_cast<const uint32_t*>(t->xr);
+        a.ll_tp = t->tp_size;
+        a.ll_rank = t->tp_rank;
+        a.ll_rows = act_rows(t);
+        a.ll_row0 = 0;
+    };
     float* xa = t->x;              // residual stream after attention's add (and the embedding)
     float* xb = t->tp ? t->x2 : t->x;  // after the ffn's add
     int rc;
@@ -517,9 +533,10 @@ int forward_launch(Transformer* t, int batch) {
         aq.max_splits = t->max_splits;
         if ((e = attn_quant_launch(aq, st, true)) != cudaSuccess) return cuda_fail(e, "attention merge + quantize");
         base(a, DQ);
-        a.seg[0] = {t->wo.q + (size_t)l * D * rbQ, t->wo.s + (size_t)l * D * ngQ, t->tp ? ywo : xa, D,
+        a.seg[0] = {t->wo.q + (size_t)l * D * rbQ, t->wo.s + (size_t)l * D * ngQ, t->tp ? t->ybuf : xa, D,
                     t->tp ? EPI_STORE : EPI_ADD};
         a.nseg = 1;
+        if (peer) push_to(a, 0);
         qin(a);
         if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "wo gemv");
         if ((rc = allreduce())) return rc;
@@ -538,9 +555,10 @@ int forward_launch(Transformer* t, int batch) {
         // 5. w2 + residual
         if ((e = quant(IN_F32, t->h1, H, nullptr)) != cudaSuccess) return cuda_fail(e, "ffn quantize");
         base(a, H);
-        a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->tp ? yw2 : xb, D,
+        a.seg[0] = {t->w2.q + (size_t)l * D * rbH, t->w2.s + (size_t)l * D * ngH, t->tp ? t->ybuf : xb, D,
                     t->tp ? EPI_STORE : EPI_ADD};
         a.nseg = 1;
+        if (peer) push_to(a, 1);
         qin(a);
         if ((e = product_rows(t, a, batch, st)) != cudaSuccess) return cuda_fail(e, "w2 gemv");
         if ((rc = allreduce())) return rc;
@@ -731,7 +749,7 @@ void tp_local_shape(const Transformer* t, const LqTensorDesc& d, int64_t* rows, 
 int xr_setup(Transformer* t) {
     const int size = t->tp_size, rank = t->tp_rank;
     if (size > lq::kTpMax) return lq_fail(LQ_EUNSUPPORTED, "peer all-reduce over %d GPUs (at most %d)", size, lq::kTpMax);
-    const size_t bytes = lq::kXrFlagsBytes + lq::kXrCountersBytes + 2 * xr_slot_bytes(t);
+    const size_t bytes = lq::kXrCountersBytes + 2 * xr_slot_bytes(t);
     cudaError_t e = cudaMalloc(&t->xr, bytes);
     if (e != cudaSuccess) return cuda_fail(e, "exchange region");
     cudaStream_t st = nullptr;
@@ -1111,11 +1129,11 @@ int forward_batch_argmax(Transformer* t, const int* tokens, const int* pos, int 
 int lq_tp_wait_selftest(int tp_size, int wait_us, double* first_ms, double* second_ms) {
     if (tp_size < 2 || tp_size > lq::kTpMax || wait_us < 1 || wait_us > 10000000)
         return lq_fail(LQ_EINVAL, "lq_tp_wait_selftest: tp_size in [2, %d], wait_us in [1, 1e7]", lq::kTpMax);
-    // rank 0 of a tp_size group whose other members never publish: every
-    // process's exchange region lives on this device and only rank 0 runs
+    // rank 0 of a tp_size group whose other members never push: its own
+    // counters and slot live on this device, the other ranks' words stay 0
     const int n = 256, gs = 64, ng = n / gs;
-    const size_t region = lq::kXrFlagsBytes + lq::kXrCountersBytes + 2 * (size_t)n * sizeof(float);
-    const size_t bytes = tp_size * region + 4 * (size_t)n * sizeof(float) + n + 2 * ng * 4 + 256;
+    const size_t slot = (size_t)tp_size * n * sizeof(uint64_t);
+    const size_t bytes = lq::kXrCountersBytes + slot + 4 * (size_t)n * sizeof(float) + n + 2 * ng * 4 + 256;
     char* buf = nullptr;
     cudaStream_t st = nullptr;
     cudaEvent_t ev[3] = {};
@@ -1125,7 +1143,7 @@ int lq_tp_wait_selftest(int tp_size, int wait_us, double* first_ms, double* seco
     for (int i = 0; i < 3 && e == cudaSuccess; ++i) e = cudaEventCreate(&ev[i]);
     int rc = LQ_OK;
     if (e == cudaSuccess) {
-        char* p = buf + tp_size * region;
+        char* p = buf + lq::kXrCountersBytes + slot;
         float* x = reinterpret_cast<float*>(p);
         float* w = x + n;
         float* xo = w + n;
@@ -1143,13 +1161,9 @@ int lq_tp_wait_selftest(int tp_size, int wait_us, double* first_ms, double* seco
         a.q.xs = reinterpret_cast<float*>(reinterpret_cast<char*>(a.q.xq) + n);
         a.q.xsum = reinterpret_cast<int*>(a.q.xs + ng);
         a.err = reinterpret_cast<int*>(a.q.xsum + ng);
-        for (int r = 0; r < tp_size; ++r) {
-            char* base = buf + r * region;
-            a.peer_slot[r] = reinterpret_cast<const float*>(base + lq::kXrFlagsBytes + lq::kXrCountersBytes);
-            a.peer_flag[r] = reinterpret_cast<uint32_t*>(base);  // rank 0's entry of process r's flags
-        }
-        a.my_flags = reinterpret_cast<const uint32_t*>(buf);
-        a.counters = reinterpret_cast<uint32_t*>(buf + lq::kXrFlagsBytes);
+        a.counters = reinterpret_cast<uint32_t*>(buf);
+        a.slot = reinterpret_cast<const uint64_t*>(buf + lq::kXrCountersBytes);
+        a.ll_rows = 1;
         a.tp_rank = 0;
         a.tp_size = tp_size;
         a.wait_ns = (uint64_t)wait_us * 1000ull;
