@@ -20,6 +20,16 @@ uint64_t* g_trace = nullptr;  // device buffer for per-CTA GEMV phase timestamps
 std::mutex g_ctx_mu;
 lq::DevCtx* g_ctx[64] = {nullptr};
 
+// page-locked (registered or cudaHostAlloc'd) host memory
+bool is_pinned_host_ptr(const void* p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return at.type == cudaMemoryTypeHost;
+}
+
 bool is_device_ptr(const void* p) {
     cudaPointerAttributes at;
     if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
@@ -70,6 +80,10 @@ int ensure_scratch(DevCtx* c, size_t bytes) {
         return lq_fail(LQ_EINVAL,
                        "scratch of %zu bytes needed inside a graph capture: make one call of this size before capturing",
                        bytes);
+    // the cached call graphs point into the old scratch
+    for (auto& g : c->graphs)
+        if (g.exec) cudaGraphExecDestroy(g.exec);
+    c->graphs.clear();
     if (c->scratch) cudaFree(c->scratch);
     c->scratch = nullptr;
     c->scratch_bytes = 0;
@@ -396,27 +410,94 @@ int matmul_f32(float* xout, const float* x, const QuantizedTensor* w, int n, int
     rc = ensure_scratch(c, off_xsum + up((size_t)ng * 4));
     if (rc) return rc;
     char* sc = static_cast<char*>(c->scratch);
-    const float* xd = x;
     float* yd = ydev ? xout : reinterpret_cast<float*>(sc + off_y);
-    if (!xdev) {
-        cudaError_t e = cudaMemcpyAsync(sc, x, (size_t)n * 4, cudaMemcpyHostToDevice, g_stream);
-        if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of x");
-        xd = reinterpret_cast<const float*>(sc);
+    // the call's work on stream st: copy x in (host x), the activation
+    // quantizer (quantize_act, runq.c:117-139), then the GEMV from the int8
+    // activation (it streams its first weights while the quantizer runs),
+    // copy y out (host y)
+    auto enqueue = [&](cudaStream_t st, bool pdl_first) -> int {
+        const float* xd = x;
+        if (!xdev) {
+            cudaError_t e = cudaMemcpyAsync(sc, x, (size_t)n * 4, cudaMemcpyHostToDevice, st);
+            if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of x");
+            xd = reinterpret_cast<const float*>(sc);
+        }
+        int r = lq::matmul_f32_device(yd, xd, w, n, d, reinterpret_cast<int8_t*>(sc + off_xq),
+                                      reinterpret_cast<float*>(sc + off_xs), reinterpret_cast<int*>(sc + off_xsum),
+                                      c->err, st, pdl_first, c->num_sms, g_trace);
+        if (r) return r;
+        if (!ydev) {
+            cudaError_t e = cudaMemcpyAsync(xout, yd, (size_t)d * 4, cudaMemcpyDeviceToHost, st);
+            if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: copy of y");
+        }
+        return LQ_OK;
+    };
+    auto finish = [&]() -> int {
+        if (xdev && ydev) return LQ_OK;  // device buffers: asynchronous like matmul
+        cudaError_t e = cudaStreamSynchronize(g_stream);
+        return e == cudaSuccess ? LQ_OK : cuda_fail(e, "matmul_f32");
+    };
+    // page-locked host x and y: one graph launch per call from the second
+    // call with the same buffers, weight and shape on
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    const bool graphable = !xdev && !ydev && !g_trace && is_pinned_host_ptr(x) && is_pinned_host_ptr(xout) &&
+                           cudaStreamIsCapturing(g_stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone;
+    if (graphable) {
+        DevCtx::CallGraph* g = nullptr;
+        for (auto& k : c->graphs)
+            if (k.x == x && k.y == xout && k.wq == w->q && k.ws == w->s && k.kind == w->kind &&
+                k.gs == w->group_size && k.n == n && k.d == d && k.flags == g_launch_flags) {
+                g = &k;
+                break;
+            }
+        if (g && g->exec) {
+            g->used = ++c->tick;
+            cudaError_t e = cudaGraphLaunch(g->exec, g_stream);
+            if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: graph launch");
+            return finish();
+        }
+        if (g && !g->failed) {
+            // second call with this key: capture the call on the private stream
+            if (!c->capture && cudaStreamCreateWithFlags(&c->capture, cudaStreamNonBlocking) != cudaSuccess) {
+                cudaGetLastError();
+                c->capture = nullptr;
+            }
+            cudaGraph_t graph = nullptr;
+            cudaGraphExec_t exec = nullptr;
+            bool ok = c->capture && cudaStreamBeginCapture(c->capture, cudaStreamCaptureModeThreadLocal) == cudaSuccess;
+            if (ok) {
+                ok = enqueue(c->capture, false) == LQ_OK;
+                ok = cudaStreamEndCapture(c->capture, &graph) == cudaSuccess && ok;
+            }
+            ok = ok && cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+            if (graph) cudaGraphDestroy(graph);
+            if (!ok) {
+                cudaGetLastError();
+                if (exec) cudaGraphExecDestroy(exec);
+                g->failed = true;  // this key runs call by call from now on
+            } else {
+                g->exec = exec;
+                g->used = ++c->tick;
+                cudaError_t e = cudaGraphLaunch(exec, g_stream);
+                if (e != cudaSuccess) return cuda_fail(e, "matmul_f32: graph launch");
+                return finish();
+            }
+        } else if (!g) {
+            // first call with this key: remember it (64 keys, least recently used dropped)
+            if (c->graphs.size() >= 64) {
+                auto old = c->graphs.begin();
+                for (auto it = c->graphs.begin(); it != c->graphs.end(); ++it)
+                    if (it->used < old->used) old = it;
+                if (old->exec) cudaGraphExecDestroy(old->exec);
+                c->graphs.erase(old);
+            }
+            c->graphs.push_back({x, xout, w->q, w->s, w->kind, w->group_size, n, d, g_launch_flags, nullptr, false,
+                                 ++c->tick});
+        }
     }
-    // the activation quantizer (quantize_act, runq.c:117-139), then the GEMV
-    // from the int8 activation; the GEMV streams its first weights while the
-    // quantizer runs
-    rc = lq::matmul_f32_device(yd, xd, w, n, d, reinterpret_cast<int8_t*>(sc + off_xq),
-                               reinterpret_cast<float*>(sc + off_xs), reinterpret_cast<int*>(sc + off_xsum), c->err,
-                               g_stream, g_launch_flags & LQ_LAUNCH_PDL, c->num_sms, g_trace);
+    rc = enqueue(g_stream, g_launch_flags & LQ_LAUNCH_PDL);
     if (rc) return rc;
-    if (!xdev || !ydev) {
-        cudaError_t e = cudaSuccess;
-        if (!ydev) e = cudaMemcpyAsync(xout, yd, (size_t)d * 4, cudaMemcpyDeviceToHost, g_stream);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(g_stream);
-        if (e != cudaSuccess) return cuda_fail(e, "matmul_f32");
-    }
-    return LQ_OK;
+    return finish();
 }
 
 }  // extern "C"

@@ -4,6 +4,8 @@
 #include <cstdint>
 #include <cuda_runtime.h>
 
+#include <vector>
+
 #include "lq_host.h"
 
 namespace lq {
@@ -19,6 +21,23 @@ struct DevCtx {
     int* qg_cnt = nullptr;      // per-tile arrival counters (left zero by every launch)
     float* qg_xst = nullptr;    // transposed activation scales [ng][64]
     size_t qg_xst_floats = 0;
+    // matmul_f32 with page-locked host x and y: the call's copy in, quantize,
+    // GEMV and copy out replayed as one CUDA graph per (buffers, weight,
+    // shape); built on the second call with the same key, dropped whenever
+    // the scratch the graphs use is reallocated
+    struct CallGraph {
+        const void* x;
+        void* y;
+        const void* wq;
+        const float* ws;
+        int kind, gs, n, d, flags;
+        cudaGraphExec_t exec;  // null until built (or when building failed)
+        bool failed;
+        uint64_t used;
+    };
+    std::vector<CallGraph> graphs;
+    cudaStream_t capture = nullptr;  // private stream the graphs are captured on
+    uint64_t tick = 0;
 };
 
 DevCtx* ctx();  // context of the current device (created on first use)

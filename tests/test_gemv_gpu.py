@@ -129,6 +129,33 @@ def test_matmul_f32_host_and_device(cuda, kind):
     assert np.array_equal(yd.cpu().numpy(), out)
 
 
+@pytest.mark.parametrize("kind", [8, 4])
+def test_matmul_f32_repeated_pinned_calls(cuda, kind):
+    """Page-locked host x and y passed again and again (the end-to-end
+    pattern): the first call runs operation by operation, the second builds
+    the call's graph, later calls replay it.  Every call reads the current x
+    and equals the device-buffer call bit for bit; a second weight with the
+    same buffers gets its own result."""
+    d, n, gs = 1024, 4096, 64
+    rng = np.random.default_rng(17 + kind)
+    wq, ws = _weights(rng, d, n, gs, kind)
+    wq2, ws2 = _weights(rng, d, n, gs, kind)
+    w, keep_w = weight_tensor(cuda, wq, ws, n, gs, kind)
+    w2, keep_w2 = weight_tensor(cuda, wq2, ws2, n, gs, kind)
+    hx = cuda.empty(n, dtype=cuda.float32).pin_memory()
+    hy = cuda.empty(d, dtype=cuda.float32).pin_memory()
+    yd = cuda.empty(d, dtype=cuda.float32, device="cuda")
+    for i in range(5):
+        wi = w2 if i == 3 else w
+        x = rng.standard_normal(n).astype(np.float32)
+        hx.copy_(cuda.from_numpy(x))
+        hy.fill_(float("nan"))
+        lq.matmul_f32(hy.data_ptr(), hx.data_ptr(), wi, n, d)
+        lq.matmul_f32(yd.data_ptr(), dev(cuda, x).data_ptr(), wi, n, d)
+        lq.sync()
+        assert np.array_equal(hy.numpy(), yd.cpu().numpy()), i
+
+
 def test_matmul_is_deterministic(cuda):
     d, n, gs, kind = 11008, 4096, 64, 4
     rng = np.random.default_rng(1)
