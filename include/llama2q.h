@@ -227,8 +227,9 @@ int forward_batch_argmax(Transformer* t, const int* tokens, const int* pos, int 
  * Attention, RoPE, the KV cache and SwiGLU stay local; the wo and w2 products
  * are partial sums, completed by an all-reduce per product (two per layer)
  * inside the captured decode graph.  The all-reduce is fused into the next
- * activation quantizer: it reads the peers' partials from their device memory
- * over NVLink (CUDA IPC mappings set up when the model is built).  Setting
+ * activation quantizer: the wo / w2 products push their partial values into
+ * every process's device memory over NVLink (CUDA IPC mappings set up when the
+ * model is built) and the quantizer sums them once they have arrived.  Setting
  * LQ_TP_ALLREDUCE=nccl before building selects an ncclAllReduce instead.  At
  * most 8 processes, dim at most 8192, at most 1024 sequences a step.  The
  * embedding, the norms and the classifier are replicated, so every process

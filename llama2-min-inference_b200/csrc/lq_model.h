@@ -55,6 +55,7 @@ struct Transformer {
     // process's region as mapped here (rank order, own one included); with
     // tp_nccl set (LQ_TP_ALLREDUCE=nccl) the step all-reduces ybuf with NCCL
     void* xr = nullptr;
+    int xr_rows = 0;                     // slot rows of the exchange region (activation rows at set-up)
     void* xr_peer[8] = {};
     bool tp_nccl = false;
     uint64_t tp_wait_ns = 0;             // peer flag wait limit (LQ_TP_WAIT_MS; 0 = the 2 s default)

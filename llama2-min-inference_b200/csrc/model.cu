@@ -48,9 +48,10 @@ constexpr int kPromptRows = 64;  // prompt tokens per prefill step (forward_prom
 // prompt chunk is up to kPromptRows rows of one sequence)
 int act_rows(const Transformer* t) { return t->max_batch > kPromptRows ? t->max_batch : kPromptRows; }
 
-// one slot of the peer all-reduce exchange region: [tp][act_rows][dim] 64-bit words
+// one slot of the peer all-reduce exchange region: [tp][xr_rows][dim] 64-bit
+// words, xr_rows = the activation rows when the region was set up
 size_t xr_slot_bytes(const Transformer* t) {
-    return (size_t)t->tp_size * act_rows(t) * t->c.dim * sizeof(uint64_t);
+    return (size_t)t->tp_size * t->xr_rows * t->c.dim * sizeof(uint64_t);
 }
 // slot k of the exchange region at `base` (this process's or a peer's mapping)
 uint64_t* xr_slot(const Transformer* t, void* base, int k) {
@@ -459,7 +460,7 @@ int forward_launch(Transformer* t, int batch) {
             p.q.xs_t_mul = kind == LQ_KIND_INT4 ? 0.0625f : 1.0f;
         }
         p.slot = xr_slot(t, t->xr, k);
-        p.ll_rows = act_rows(t);
+        p.ll_rows = t->xr_rows;
         p.counters = static_cast<uint32_t*>(t->xr);
         p.tp_rank = t->tp_rank;
         p.tp_size = t->tp_size;
@@ -477,7 +478,7 @@ int forward_launch(Transformer* t, int batch) {
         a.ll_call = static_cast<const uint32_t*>(t->xr);
         a.ll_tp = t->tp_size;
         a.ll_rank = t->tp_rank;
-        a.ll_rows = act_rows(t);
+        a.ll_rows = t->xr_rows;
         a.ll_row0 = 0;
     };
     float* xa = t->x;              // residual stream after attention's add (and the embedding)
@@ -749,6 +750,7 @@ void tp_local_shape(const Transformer* t, const LqTensorDesc& d, int64_t* rows, 
 int xr_setup(Transformer* t) {
     const int size = t->tp_size, rank = t->tp_rank;
     if (size > lq::kTpMax) return lq_fail(LQ_EUNSUPPORTED, "peer all-reduce over %d GPUs (at most %d)", size, lq::kTpMax);
+    t->xr_rows = act_rows(t);
     const size_t bytes = lq::kXrCountersBytes + 2 * xr_slot_bytes(t);
     cudaError_t e = cudaMalloc(&t->xr, bytes);
     if (e != cudaSuccess) return cuda_fail(e, "exchange region");
@@ -1106,7 +1108,15 @@ int transformer_reserve_batch(Transformer* t, int max_batch) {
     free_state(t);
     t->max_batch = max_batch;
     cudaGetLastError();
-    return alloc_state(t);
+    int rc = alloc_state(t);
+    // the peer all-reduce's exchange region holds a slot row per activation
+    // row: set it up again (collectively: every process makes this call with
+    // the same arguments) when the new activation rows exceed it
+    if (!rc && t->xr && act_rows(t) > t->xr_rows) {
+        xr_teardown(t);
+        rc = xr_setup(t);
+    }
+    return rc;
 }
 
 float* forward_batch(Transformer* t, const int* tokens, const int* pos, int batch) {

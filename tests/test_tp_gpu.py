@@ -90,9 +90,11 @@ def _tp_rank(rank, world, gid, kind, q, mode, env):
         elif mode == "batch":
             t = L.Transformer.random_tp(L.Config.make(*TP_CONF), kind, 64, SEED, rank, world, gid, 64)
             out = np.stack([t.forward(tok, pos).copy() for pos, tok in enumerate(TP_TOKENS)])
-            t.reserve_batch(16)
-            tokb = np.arange(16, dtype=np.int32) * 31 + 1
-            outb = np.stack([t.forward_batch(tokb, np.full(16, p, np.int32)).copy() for p in range(3)])
+            # 80 rows: more than the 64 the exchange region was set up for (it is
+            # set up again), two tensor-core chunks (slot rows 0-63, 64-79)
+            t.reserve_batch(80)
+            tokb = (np.arange(80, dtype=np.int32) * 31 + 1) % TP_CONF[5]
+            outb = np.stack([t.forward_batch(tokb, np.full(80, p, np.int32)).copy() for p in range(3)])
             t.close()
             q.put((rank, out, outb))
         elif mode == "stop":
@@ -156,8 +158,10 @@ def test_tp_equals_tp_oracle(cuda, world, kind):
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("kind", [8, 4])
 def test_tp_peer_allreduce_vs_nccl(cuda, world, kind):
-    """Batch 1 (GEMV) and batch 16 (tensor-core GEMM) steps: the peer
-    all-reduce fused into the quantizer against the NCCL all-reduce.  With 2
+    """Batch 1 (GEMV) and batch 80 (tensor-core GEMM in chunks of 64 and 16
+    rows, after a batch reservation beyond the rows the exchange region was
+    first set up for) steps: the peer all-reduce fused into the quantizer
+    against the NCCL all-reduce.  With 2
     processes both sums are y_0 + y_1, so the logits are bitwise equal; with
     more, NCCL may associate the sum differently, so the logits agree to
     fp32 rounding until an int8 activation flips (argmax agreement checked)."""
