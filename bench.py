@@ -581,14 +581,24 @@ def tp_bench(lq, torch, rank, world, dist, ctx: int = 2048, steps1: int = 16, st
     return out
 
 
+PROBE_SHAPES = {  # dim, hidden, heads, kv heads of the Llama-2 layer shapes
+    "13b": (5120, 13824, 40, 40),
+    "70b": (8192, 28672, 64, 8),
+    "7b": (4096, 11008, 32, 32),
+}
+
+
 def probe(spec: str):
-    """One small decode case for profilers: "LAYERS:BATCH:KIND:CTX" on the
-    Llama-2-13B layer shape (3 warm steps, 1 timed step, printed in ms)."""
+    """One small decode case for profilers: "LAYERS:BATCH:KIND:CTX[:SHAPE]"
+    on a Llama-2 layer shape (13b by default, or 70b / 7b); 3 warm steps, 1
+    timed step, printed in ms."""
     import torch
 
-    L, B, kind, ctx = (int(v) for v in spec.split(":"))
+    f = spec.split(":")
+    L, B, kind, ctx = (int(v) for v in f[:4])
+    D, H, NH, NKV = PROBE_SHAPES[f[4] if len(f) > 4 else "13b"]
     lq = importlib.import_module("llama2-min-inference_b200")
-    t = lq.Transformer.random(lq.Config.make(5120, 13824, L, 40, 40, 32000, 4096), kind, 64, 11, ctx + 16)
+    t = lq.Transformer.random(lq.Config.make(D, H, L, NH, NKV, 32000, 4096), kind, 64, 11, ctx + 16)
     t.reserve_batch(B)
     tok = np.ones(B, np.int32)
     for w in range(3):
@@ -815,7 +825,7 @@ def main():
     ap.add_argument("--no-batch", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--no-per-shape", action="store_true")
-    ap.add_argument("--probe", default=None, help="LAYERS:BATCH:KIND:CTX: one small 13B-shape step for profilers")
+    ap.add_argument("--probe", default=None, help="LAYERS:BATCH:KIND:CTX[:13b|70b|7b]: one small decode step for profilers")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
