@@ -968,7 +968,8 @@ __global__ void __launch_bounds__(kAqThreads) act_quant_kernel(const __grid_cons
     float inv = 1.0f;
     if (norm) {
         // rmsnorm sum of squares: thread t takes float4 chunks t, t+256, ...
-        constexpr int U = 4;
+        // (all of a row of up to 8192 values loaded at once)
+        constexpr int U = 8;
         float ss = 0.0f;
         for (int c0 = ctid; c0 < n / 4; c0 += U * kAqThreads) {
             float4 v[U];
@@ -1070,6 +1071,13 @@ __global__ void __launch_bounds__(kAqThreads) attn_quant_kernel(const __grid_con
         float* lw = msm + nhc * ms;  // [nhc][ms]
         float* Ls = lw + nhc * ms;   // [nhc]
         const float* prow = aa.part + (size_t)b * (n / hs) * ms * ps;
+        // this thread's output's chunk values: the first batch is loaded
+        // before the per-head weights are known, so both wait for one round
+        const int hh_k = k / hs - h0, d_k = k - (k / hs) * hs;
+        const float* src = prow + (size_t)(h0 + hh_k) * ms * ps + 4 + d_k;
+        float x[kMergeBatch];
+#pragma unroll
+        for (int u = 0; u < kMergeBatch; ++u) x[u] = on && u < nsplit ? __ldcg(src + (size_t)u * ps) : 0.0f;
         for (int i = tid; i < nhc * nsplit; i += kAqThreads) {
             const int hh = i / nsplit, s2 = i - hh * nsplit;
             const float2 m_l = __ldcg(reinterpret_cast<const float2*>(prow + ((size_t)(h0 + hh) * ms + s2) * ps));
@@ -1091,19 +1099,19 @@ __global__ void __launch_bounds__(kAqThreads) attn_quant_kernel(const __grid_con
         }
         __syncthreads();
         if (on) {
-            const int hh = k / hs - h0, d = k - (k / hs) * hs;
-            const float* src = prow + (size_t)(h0 + hh) * ms * ps + 4 + d;
-            const float* w = mw + hh * ms;
+            const float* w = mw + hh_k * ms;
             float o = 0.0f;
             for (int s0 = 0; s0 < nsplit; s0 += kMergeBatch) {
-                float x[kMergeBatch];
+                if (s0 > 0) {
 #pragma unroll
-                for (int u = 0; u < kMergeBatch; ++u) x[u] = s0 + u < nsplit ? __ldcg(src + (size_t)(s0 + u) * ps) : 0.0f;
+                    for (int u = 0; u < kMergeBatch; ++u)
+                        x[u] = s0 + u < nsplit ? __ldcg(src + (size_t)(s0 + u) * ps) : 0.0f;
+                }
 #pragma unroll
                 for (int u = 0; u < kMergeBatch; ++u)
                     if (s0 + u < nsplit) o = fmaf(x[u], w[s0 + u], o);
             }
-            v = o / Ls[hh];
+            v = o / Ls[hh_k];
         }
     }
     // quantize as quant_task8 does: group absmax, scale amax / 127, values

@@ -183,22 +183,30 @@ __global__ void __launch_bounds__(NT, 1024 / NT) attention_kernel(const __grid_c
             if (tid == 0) mbar_wait(&kv_bar, 0, a.err, DEV_TIMEOUT_DRAIN);
             return;
         }
-        const int jl = head_of_lane<KM>(lane);
-        const bool writer = (lane & (32 / KM - 1)) == 0;
-        for (int t = warp; t < nt; t += NW) {
-            float acc[KM];
+        // a pass of a warp takes P = 8 / KM positions: 8 dot products (P
+        // positions x KM heads) reduced together; lane group v = lane / 4
+        // ends with dot v = (position p, head j), v = p * KM + j
+        constexpr int P = 8 / KM;
+        const int v = head_of_lane<8>(lane), pv = v / KM, jv = v - pv * KM;
+        const bool writer = (lane & 3) == 0;
+        for (int t0w = warp * P; t0w < nt; t0w += NW * P) {
+            float acc[8];
 #pragma unroll
-            for (int j = 0; j < KM; ++j) acc[j] = 0.0f;
+            for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
 #pragma unroll
             for (int m = 0; m < 4; ++m) {
                 if (lane + 32 * m < hs) {
-                    const float kv = kval(t, m);
 #pragma unroll
-                    for (int j = 0; j < KM; ++j) acc[j] = fmaf(qr[j][m], kv, acc[j]);
+                    for (int p = 0; p < P; ++p) {
+                        // rows past the chunk's positions hold other data: read, never stored
+                        const float kv = kval(t0w + p < kChunk ? t0w + p : kChunk - 1, m);
+#pragma unroll
+                        for (int j = 0; j < KM; ++j) acc[p * KM + j] = fmaf(qr[j][m], kv, acc[p * KM + j]);
+                    }
                 }
             }
-            const float dot = multi_warp_sum<KM>(acc, lane);
-            if (writer) sc[jl * kChunk + t] = dot / rs;
+            const float dot = multi_warp_sum<8>(acc, lane);
+            if (writer && t0w + pv < nt) sc[jv * kChunk + t0w + pv] = dot / rs;
         }
     } else {
         for (int i = tid; i < km * hs; i += NT) qs[i] = qg[i];
