@@ -377,11 +377,45 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float* __restrict__ 
     const float* v = logits + (size_t)blockIdx.x * stride;
     float bv = -FLT_MAX;
     int bi = -1;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float x = v[i];
+    // each thread scans its elements in increasing index order; the loads of
+    // a pass (8 float4, or 8 scalars when the row is not 16-byte aligned) are
+    // issued before the compares
+    auto take = [&](float x, int i) {
         if (bi < 0 || x > bv) {
             bv = x;
             bi = i;
+        }
+    };
+    if ((reinterpret_cast<uintptr_t>(v) & 15u) == 0) {
+        const int n4 = n / 4;
+        const float4* v4 = reinterpret_cast<const float4*>(v);
+        for (int c0 = threadIdx.x; c0 < n4; c0 += 8 * blockDim.x) {
+            float4 x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + u * blockDim.x;
+                x[u] = c < n4 ? v4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < 8; ++u) {
+                const int c = c0 + u * blockDim.x;
+                if (c < n4) {
+                    take(x[u].x, 4 * c);
+                    take(x[u].y, 4 * c + 1);
+                    take(x[u].z, 4 * c + 2);
+                    take(x[u].w, 4 * c + 3);
+                }
+            }
+        }
+        for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) take(v[i], i);
+    } else {
+        for (int i0 = threadIdx.x; i0 < n; i0 += 8 * blockDim.x) {
+            float x[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) x[u] = i0 + u * blockDim.x < n ? v[i0 + u * blockDim.x] : 0.0f;
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+                if (i0 + u * blockDim.x < n) take(x[u], i0 + u * blockDim.x);
         }
     }
     __shared__ float sv[32];
