@@ -216,8 +216,12 @@ def matmul(xout_ptr: int, x: QuantizedTensor, w: QuantizedTensor, n: int, d: int
 
 
 def matmul_f32(xout_ptr: int, x_ptr: int, w: QuantizedTensor, n: int, d: int) -> None:
-    """quantize_act + matmul_q8 in one call; host or device pointers."""
-    check(lib().matmul_f32(C.c_void_p(xout_ptr), C.c_void_p(x_ptr), C.byref(w), n, d))
+    """quantize_act + matmul_q8 in one call; host or device pointers.  (The
+    pointers go to the C function as plain integers and the weight by
+    reference, through the argument types set when the library was loaded.)"""
+    rc = lib().matmul_f32(xout_ptr, x_ptr, w, n, d)
+    if rc != OK:
+        raise LlamaQError(rc, last_error())
 
 
 def matmul_f32_noalloc(xout_ptr: int, x_ptr: int, w: QuantizedTensor, n: int, d: int) -> None:
