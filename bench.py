@@ -372,6 +372,8 @@ def decode_bench(lq, torch, positions: int = 2048):
             "positions": positions, "tok_s": round(positions / dt, 2), "ms_per_token": round(1e3 * dt / positions, 4),
             "weight_bytes_per_token": wbytes, "avg_kv_bytes_per_token": int(kv_avg),
             "hbm_gbs_effective": round((wbytes + kv_avg) * positions / dt / 1e9, 1),
+            "roofline_frac": round((wbytes + kv_avg) * positions / dt / 1e9 / peaks()[0], 4),
+            "roofline": "(weight + average KV bytes per token) x tok/s / measured HBM peak",
             "timing": "host wall clock around forward_argmax calls (H2D token/pos, graph, D2H 4 bytes each)",
             "init_s": round(init_s, 2),
             "step_breakdown_last_position": breakdown}
@@ -421,7 +423,8 @@ def batch_bench(lq, torch, batches=(1, 8, 16, 32, 64), ctx: int = 1024, steps: i
             path = "tcgen05 kind::i8" if (B >= 16 and mma_env is None) else "dp4a GEMV"
             out["runs"].append({"weight_kind": "int%d" % kind, "batch": B, "path": path, "tok_s": round(B / dt, 1),
                                 "ms_per_step": round(1e3 * dt, 3), "weight_bytes": int(wbytes),
-                                "kv_bytes_per_step": int(kv), "hbm_gbs_effective": round(gbs, 1)})
+                                "kv_bytes_per_step": int(kv), "hbm_gbs_effective": round(gbs, 1),
+                                "roofline_frac": round(gbs / peaks()[0], 4)})
         t.close()
     return out
 
