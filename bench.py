@@ -313,7 +313,8 @@ def step_breakdown(lq, t, tokens, pos):
     transformer_trace): the step's device time and, per kernel kind, the
     launch count, the time on the step's critical path (end of the kernel
     minus end of the one before it, in launch order) and the time from its
-    dependency release to its end.  Tracing is switched off again after."""
+    dependency release to its end; and the first 24 kernels one by one.
+    Tracing is switched off again after."""
     import numpy as np
 
     t.trace(True)
@@ -344,6 +345,16 @@ def step_breakdown(lq, t, tokens, pos):
         d["critical_us"] = round(d["critical_us"], 2)
         d["busy_us"] = round(d["busy_us"], 2)
     out["by_kind"] = by
+    # the first kernels one by one: [kind, first CTA start, first CTA past its
+    # dependency wait, last CTA end], in us after the previous kernel's end
+    first, prev = [], t0
+    for i in range(min(24, len(kinds))):
+        if not valid[i]:
+            continue
+        name = lq.TRACE_KINDS.get(int(kinds[i]), str(kinds[i]))
+        first.append([name] + [round((st[i, j] - prev) / 1e3, 2) for j in range(3)])
+        prev = max(prev, st[i, 2])
+    out["first_kernels_us"] = first
     return out
 
 
